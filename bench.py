@@ -1,0 +1,486 @@
+#!/usr/bin/env python
+"""Benchmark of the tensor-core GEMM path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: the sharded int8 GEMM, M = N = K = 32768 in total, int8 uniform
+[-128, 127] from a seed, int32 accumulation and output.  A is row-partitioned
+across the ranks (M/G rows each), B is replicated, each rank computes its
+M/G x N slice of C (no data-path collective; ``--gather`` adds the optional
+all-gather of C).  The total problem is fixed, so scaling is "strong"; at one
+GPU this is the full 32768^3 problem on one B200.
+
+A "step" is one GEMM of each rank's slice.  ``value`` is whole-job TOPS with
+inputs resident in HBM (inputs are 2 GiB, larger than L2, so no flush is
+needed); ``e2e`` is the same metric through the public Python API with the
+step's A slice and B copied from pinned host memory and its C slice copied
+back inside the timed region.  Device time is measured with CUDA events on
+the launching stream, max over ranks.
+
+``--impl reference`` times the reference's own CPU GEMM (src/data_int8.cu
+cpu_gemm_int8, compiled unchanged into oracle/_ref/) on a bounded row sample
+of the same workload with all host threads; only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "GEMM TFLOPS(fp16)/TOPS(int8,int4) per B200 + % dense tensor peak; 8-GPU agg"
+SIZE = 32768
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--size", type=int, default=SIZE, help="M = N = K of the whole problem")
+    ap.add_argument("--gather", action="store_true", help="all-gather C over NCCL each step")
+    ap.add_argument("--no-extras", action="store_true", help="skip the per-config extras")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0,
+                    help="target wall time of one CPU-baseline sample")
+    return ap.parse_args()
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ---------------------------------------------------------------- clocks ----
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled every 200 ms."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.gpus = gpu_indices
+        self.rows = []
+        self.proc = None
+        self.t = None
+        self.active = False
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", ",".join(str(g) for g in self.gpus)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 9:
+                self.rows.append((time.time(), self.active, parts))
+
+    def mark(self, active: bool):
+        self.active = active
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:  # pragma: no cover
+                self.proc.kill()
+        if self.t is not None:
+            self.t.join(timeout=5)
+
+    def summary(self):
+        rows = [r for r in self.rows if r[1]] or self.rows
+        window = "timed" if any(r[1] for r in self.rows) else "whole run"
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"],
+                    "samples": 0}
+        sm = [float(r[2][1]) for r in rows if r[2][1].replace(".", "").isdigit()]
+        mx = [float(r[2][2]) for r in rows if r[2][2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[2][5 + i] == "Active"})
+        pw = [float(r[2][3]) for r in rows if r[2][3].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "power_w_max": max(pw) if pw else None, "samples": len(rows), "window": window}
+
+
+# -------------------------------------------------------- reference (CPU) ----
+
+def cpu_reference_sample(size, rows, threads, seed=0):
+    """Run the reference's own cpu_gemm_int8 (oracle/_ref) -- or, when the
+    reference was not available at build time, the oracle's restatement --
+    on `rows` rows of C for the size^3 int8 problem.  Returns (seconds, kind)."""
+    import numpy as np
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(seed)
+    A = rng.integers(-128, 128, (rows, size), dtype=np.int8)
+    BT = rng.integers(-128, 128, (size, size), dtype=np.int8)
+    Cs = np.zeros((rows, size), np.int32)
+    t0 = time.perf_counter()
+    if O.ref_data_lib("int8") is not None:
+        O.ref_gemm_rows("int8", A, BT, rows, size, size, Cs, 0, rows, threads=threads)
+        kind = "reference"
+    else:
+        Cs[:] = O.gemm_s8(A, BT, threads=threads)
+        kind = "port"
+    return time.perf_counter() - t0, kind
+
+
+def cpu_sample_rows(size, threads, target_s):
+    """Rows per sample so one sample takes about target_s seconds."""
+    t, _ = cpu_reference_sample(size, threads, threads)  # one row per thread
+    per_round = max(t, 1e-3)
+    rounds = max(1, int(target_s / per_round))
+    return threads * rounds
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    size = args.size
+    threads = host_threads()
+    rows = cpu_sample_rows(size, threads, min(args.cpu_seconds, 4.0))
+    times = []
+    kind = "reference"
+    for i in range(args.warmup + args.steps):
+        t, kind = cpu_reference_sample(size, rows, threads, seed=i)
+        if i >= args.warmup:
+            times.append(t)
+    ops = 2.0 * rows * size * size
+    mean_t = sum(times) / len(times)
+    tops = ops / mean_t / 1e12
+    sample = f"{rows} of {size} rows of C per step ({rows}x{size}x{size} int8 MACs), {threads} threads"
+    line = {
+        "metric": METRIC, "value": tops, "unit": "TOPS", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": mean_t * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": f"int8 GEMM M=N=K={size}, A row-sharded, B replicated, int32 C",
+                   "parallelism": f"rows{args.gpus}"},
+        "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": tops, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------- our arm ----
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import tensorcoreptx_b200 as T
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    size = args.size
+    assert size % world == 0, "size must divide evenly across ranks"
+    rows = size // world
+    ops_total = 2.0 * size * size * size
+    ops_rank = 2.0 * rows * size * size
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # inputs: A slice of this rank, full B (BT layout, N x K), seeded on the GPU
+    g = torch.Generator(device=dev).manual_seed(1234)
+    A_full_seed_offset = rank  # each rank draws its own rows of the global A
+    g.manual_seed(1234 + A_full_seed_offset)
+    A = torch.randint(-128, 128, (rows, size), generator=g, device=dev, dtype=torch.int8)
+    g.manual_seed(999)  # identical B on every rank (replicated)
+    BT = torch.randint(-128, 128, (size, size), generator=g, device=dev, dtype=torch.int8)
+    C = torch.empty(rows, size, dtype=torch.int32, device=dev)
+    C_full = torch.empty(size, size, dtype=torch.int32, device=dev) if (args.gather and world > 1) else None
+
+    from tensorcoreptx_b200 import _native as nat
+    lib = nat.lib()
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        st = lib.tcg_gemm_s8(A.data_ptr(), BT.data_ptr(), C.data_ptr(), rows, size, size, 1,
+                             nat.TCG_B_NK, stream.cuda_stream)
+        nat.check("tcg_gemm_s8", st)
+        if C_full is not None:
+            with torch.cuda.stream(stream):
+                dist.all_gather_into_tensor(C_full, C)
+
+    clocks = ClockSampler(list(range(world)) if rank == 0 else [local])
+    if rank == 0:
+        clocks.start()
+        time.sleep(0.5)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    stream.synchronize()
+
+    # ---- kernel-resident timed region
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    clocks.mark(True)
+    t_begin = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_begin.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        st = lib.tcg_gemm_s8(A.data_ptr(), BT.data_ptr(), C.data_ptr(), rows, size, size, 1,
+                             nat.TCG_B_NK, stream.cuda_stream)
+        nat.check("tcg_gemm_s8", st)
+        ev[i][1].record(stream)
+        if C_full is not None:
+            with torch.cuda.stream(stream):
+                dist.all_gather_into_tensor(C_full, C)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks.mark(False)
+    total_ms = max_over_ranks(t_begin.elapsed_time(t_end))
+    launch_ms = [a.elapsed_time(b) for a, b in ev]
+    kern_ms = max_over_ranks(sum(launch_ms) / len(launch_ms))
+    tile_n = T.last_tile_n()
+    werr = T.check_device_error(stream)
+    assert werr == 0
+
+    # ---- end-to-end through the public API: pinned host in, pinned host out
+    A_h = A.cpu().pin_memory()
+    B_h = BT.cpu().pin_memory()
+    C_h = torch.empty(rows, size, dtype=torch.int32).pin_memory()
+    del A, BT, C
+    torch.cuda.empty_cache()
+
+    def e2e_step():
+        Ad = A_h.to(dev, non_blocking=True)
+        Bd = B_h.to(dev, non_blocking=True)
+        Cd = T.gemm_int8(Ad, Bd)
+        C_h.copy_(Cd, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            e2e_step()
+    stream.synchronize()
+    e2e_steps = max(3, min(args.steps, 10))
+    barrier()
+    torch.cuda.synchronize()
+    clocks.mark(True)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks.mark(False)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
+    h2d = rows * size + size * size
+    d2h = rows * size * 4
+    del A_h, B_h, C_h
+    torch.cuda.empty_cache()
+
+    if rank == 0:
+        clocks.stop()
+
+    result = None
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        # int8 dense tensor peak = 2x the dense bf16 peak on B200 (4.5 POPS vs
+        # 2.25 PFLOP/s nominal); the kernel is timed inside a long step, so the
+        # sustained bf16 figure is the denominator.
+        peak_tops = 2.0 * float(peaks.get("bf16_tflops_sustained", 1400.0))
+        achieved = ops_rank / (kern_ms * 1e-3) / 1e12
+        traffic = profile_traffic(size, rows)
+        ms_per_step = total_ms / args.steps
+        result = {
+            "metric": METRIC,
+            "value": ops_total / (ms_per_step * 1e-3) / 1e12,
+            "unit": "TOPS",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "int8",
+            "data": "synthetic",
+            "config": {
+                "workload": f"int8 GEMM M=N=K={size}, A row-sharded over {world} GPU(s), "
+                            f"B replicated, int32 C" + (", C all-gathered" if C_full is not None else ""),
+                "per_rank": f"{rows}x{size}x{size}",
+                "values": "int8 uniform [-128,127], seeded",
+                "l2": "inputs (2 GiB) larger than L2; no flush",
+                "tile_n": tile_n,
+                "parallelism": f"rows{world}",
+            },
+            "roofline": {
+                "bound": "tensor",
+                "achieved": achieved,
+                "peak": peak_tops,
+                "unit": "TOPS",
+                "frac": achieved / peak_tops,
+                "traffic": traffic,
+                "peak_source": f"2 x bf16_tflops_sustained of MEASURED_PEAKS.json ({peak_src})",
+                "frac_of_burst": achieved / (2.0 * float(peaks.get("bf16_tflops", 1590.0))),
+            },
+            "e2e": {"value": ops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps * (1 if C_full is None else 2),
+            "clocks": clocks.summary(),
+        }
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def profile_traffic(size, rows):
+    """DRAM bytes per launch from the committed ncu summary of this kernel,
+    scaled to this launch by the MACs it processes; None when absent."""
+    path = os.path.join(ROOT, "profiles", "gemm_s8_traffic.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        per_mac = float(p["dram_bytes_per_launch"]) / float(p["macs_per_launch"])
+        return per_mac * rows * size * size
+    except (OSError, ValueError, KeyError):
+        return None
+
+
+# ----------------------------------------------------------- extras (N=1) ----
+
+def extras():
+    """Kernel-only throughput of the other benchmark configurations on this
+    GPU, for context (one-GPU runs only)."""
+    import torch
+
+    import tensorcoreptx_b200 as T
+
+    dev = torch.device("cuda", 0)
+    out = {}
+
+    def time_fn(fn, iters):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / iters
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    n = 4096
+    A = torch.randint(-128, 128, (n, n), generator=g, device=dev, dtype=torch.int8)
+    BT = torch.randint(-128, 128, (n, n), generator=g, device=dev, dtype=torch.int8)
+    ms = time_fn(lambda: T.gemm_int8(A, BT), 50)
+    out["int8_4096"] = {"tops": 2 * n ** 3 / ms / 1e9, "ms": ms}
+    try:
+        ms_lib = time_fn(lambda: torch._int_mm(A, BT.t()), 50)
+        out["int8_4096_torch_int_mm"] = {"tops": 2 * n ** 3 / ms_lib / 1e9, "ms": ms_lib}
+    except Exception as e:  # pragma: no cover
+        out["int8_4096_torch_int_mm"] = {"error": str(e)[:80]}
+    Ap = torch.randint(-128, 128, (n, n // 2), generator=g, device=dev, dtype=torch.int8)
+    Bp = torch.randint(-128, 128, (n, n // 2), generator=g, device=dev, dtype=torch.int8)
+    ws = torch.empty(T.int4_workspace_size(n, n, n), dtype=torch.uint8, device=dev)
+    ms = time_fn(lambda: T.gemm_int4(Ap, Bp, workspace=ws), 50)
+    out["int4_4096"] = {"tops": 2 * n ** 3 / ms / 1e9, "ms": ms}
+    del A, BT, Ap, Bp, ws
+    for acc in ("fp32", "fp16"):
+        for n in (512, 1024, 2048, 4096, 8192, 16384):
+            A = (torch.rand(n, n, generator=g, device=dev) * 2 - 1).half()
+            B = (torch.rand(n, n, generator=g, device=dev) * 2 - 1).half()
+            iters = 50 if n <= 4096 else 10
+            ms = time_fn(lambda: T.gemm_fp16(A, B, acc=acc), iters)
+            out[f"fp16_{acc}acc_{n}"] = {"tflops": 2 * n ** 3 / ms / 1e9, "ms": ms}
+            if acc == "fp32" and n in (512, 4096, 16384):
+                ms_lib = time_fn(lambda: torch.matmul(A, B), iters)
+                out[f"fp16_{n}_torch_matmul"] = {"tflops": 2 * n ** 3 / ms_lib / 1e9, "ms": ms_lib}
+            del A, B
+    torch.cuda.empty_cache()
+    return out
+
+
+def cpu_baseline_line(args):
+    size = args.size
+    threads = host_threads()
+    rows = cpu_sample_rows(size, threads, args.cpu_seconds)
+    t, kind = cpu_reference_sample(size, rows, threads, seed=7)
+    return {"value": 2.0 * rows * size * size / t / 1e12, "unit": "TOPS", "cores": threads,
+            "kind": kind,
+            "sample": f"{rows} of {size} rows of C ({rows}x{size}x{size} int8 MACs) in {t:.1f} s"}
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    result = run_ours(args)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank == 0 and result is not None:
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline_line(args)
+        if world == 1 and not args.no_extras:
+            result["extras"] = extras()
+        print(json.dumps(result), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

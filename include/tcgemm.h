@@ -1,0 +1,105 @@
+/*
+ * tcgemm.h -- C ABI of the B200 (sm_100a) tensor-core GEMM library
+ * (libtcgemm.so).  Plain pointers and sizes; no C++ or torch types.
+ *
+ * Every entry point computes C = A * B for `batches` independent problems,
+ * overwriting C (alpha = 1, beta = 0), and is asynchronous on `stream`
+ * (a cudaStream_t; NULL = legacy default stream).  The caller owns every
+ * buffer; the library allocates nothing except where an entry point says so.
+ *
+ * Layouts (row-major, batch b at offset b * rows * cols of each operand):
+ *   A  : M x K, K contiguous
+ *   B  : TCG_B_KN -> K x N (N contiguous)      [reference fp16 contract]
+ *        TCG_B_NK -> N x K, "BT" (K contiguous) [reference int8/int4 contract]
+ *   C  : M x N, N contiguous, 4-byte elements (float or int32)
+ * int4 operands are packed two per byte along K, low nibble = even k,
+ * K/2 bytes per row (reference src/data_int4.h:4-6).
+ *
+ * Shape and alignment rules (TCG_ERR_SHAPE / TCG_ERR_ALIGN otherwise): each
+ * TMA-loaded row must be a multiple of 16 bytes and A, B must be 16-byte
+ * aligned:  fp16 K % 8 == 0 (and N % 8 == 0 for TCG_B_KN); int8 K % 16 == 0
+ * (N % 16 == 0 for TCG_B_KN); int4 K % 32 == 0.  M and N are otherwise
+ * arbitrary (edges are zero-filled on load and masked on store).
+ *
+ * Replaces the reference's per-kernel-file plugin symbol
+ *     void launch_kernel(const half*, const half*, float*, const GemmConfig&, cudaStream_t)
+ *     void launch_kernel(const int8_t*, const int8_t*, int32_t*, const GemmConfig&, cudaStream_t)
+ * (src/solver.cu:6-7, src/solver_int8.h:7-8, src/solver_int4.h:5-6); the
+ * reference-compatible C++ symbols live in tcgemm_compat.h.
+ */
+#ifndef TCGEMM_H
+#define TCGEMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    TCG_SUCCESS = 0,
+    TCG_ERR_SHAPE = 1,       /* a dimension breaks the rules above              */
+    TCG_ERR_ALIGN = 2,       /* A or B not 16-byte aligned (C not 4-byte)       */
+    TCG_ERR_TIMEOUT = 3,     /* a device-side bounded wait gave up (see below)  */
+    TCG_ERR_CUDA = 4,        /* a CUDA runtime call failed (tcg_last_cuda_error) */
+    TCG_ERR_ARG = 5,         /* bad enum / null pointer                          */
+    TCG_ERR_UNSUPPORTED = 6, /* device is not sm_100 (B200/GB200)                */
+    TCG_ERR_WORKSPACE = 7    /* workspace too small                              */
+} tcg_status;
+
+typedef enum { TCG_ACC_F32 = 0, TCG_ACC_F16 = 1 } tcg_acc;
+typedef enum { TCG_B_KN = 0, TCG_B_NK = 1 } tcg_b_layout;
+
+/* fp16 x fp16 -> fp32 C, fp32 (TCG_ACC_F32) or fp16 (TCG_ACC_F16) accumulation.
+ * Replaces fp16 launch_kernel: kernels/fp16_wmma.cu:92-102 (fp32 acc) and
+ * kernels/fp16_ptx_fp16acc.cu:190-200 (fp16 acc, fp32 store). */
+tcg_status tcg_gemm_f16(const void* A, const void* B, float* C,
+                        int M, int N, int K, int batches,
+                        tcg_acc acc, tcg_b_layout b_layout, void* stream);
+
+/* int8 x int8 -> int32, exact.  Replaces int8 launch_kernel:
+ * kernels/int8_wmma.cu:135-145, kernels/int8_ptx_mma_k32.cu:162-172. */
+tcg_status tcg_gemm_s8(const int8_t* A, const int8_t* B, int32_t* C,
+                       int M, int N, int K, int batches,
+                       tcg_b_layout b_layout, void* stream);
+
+/* packed int4 x int4 -> int32, exact; B is always BT (N x K/2 bytes).
+ * Replaces int4 launch_kernel: kernels/int4_wmma.cu:148-158,
+ * kernels/int4_ptx_mma_k64_x4_x2nontrans_ca.cu:168-178.
+ * The operands are widened to int8 in `workspace` (tcg_gemm_s4_workspace_size
+ * bytes, 256-byte aligned) and multiplied by the int8 tensor-core path.  With
+ * workspace == NULL the library takes stream-ordered memory from the
+ * device's default memory pool for the duration of the call. */
+size_t tcg_gemm_s4_workspace_size(int M, int N, int K, int batches);
+tcg_status tcg_gemm_s4(const int8_t* A_packed, const int8_t* BT_packed, int32_t* C,
+                       int M, int N, int K, int batches,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Widen packed int4 to int8 (low nibble first), n_packed bytes -> 2*n_packed.
+ * The first stage of tcg_gemm_s4, exposed for reuse. */
+tcg_status tcg_unpack_s4(const int8_t* packed, int8_t* out, size_t n_packed, void* stream);
+
+/* Device-side failure word.  Every wait inside the GEMM kernel is bounded
+ * (default 2 s, tcg_set_wait_timeout_ns); on expiry the kernel records
+ * (code << 32 | detail) here, drains its own copies in flight, frees its
+ * tensor memory and returns.  tcg_check_device_error synchronises `stream`,
+ * reads the word of the current device, clears it, and returns
+ * TCG_ERR_TIMEOUT if it was set (detail in *word when word != NULL). */
+tcg_status tcg_check_device_error(void* stream, uint64_t* word);
+void tcg_set_wait_timeout_ns(uint64_t ns);
+
+/* Tile width override for tuning (0 = automatic; else 64, 128 or 256). */
+void tcg_set_tile_n(int bn);
+
+/* Introspection: last CUDA error code seen, status names, library version,
+ * and the tile width chosen by the most recent launch on this thread. */
+int tcg_last_cuda_error(void);
+const char* tcg_status_string(tcg_status s);
+int tcg_version(void);
+int tcg_last_tile_n(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TCGEMM_H */

@@ -1,0 +1,373 @@
+// tcg_gemm_kernel.cuh -- the one tcgen05 GEMM mainloop behind every precision.
+//
+// Replaces all of the reference's per-variant Ada kernels (kernels/fp16_*.cu,
+// kernels/int8_*.cu and, after widening to int8, kernels/int4_*.cu) with one
+// Blackwell-native design:
+//
+//   * persistent CTAs (grid <= #SMs), static round-robin over output tiles,
+//     grouped rasterisation (kGroupM tile-rows per band) for L2 reuse;
+//   * warp specialisation, 192 threads:
+//       warp 0 lane 0  -- TMA producer: 128-byte-swizzled A and B tiles into a
+//                         kStages-deep shared-memory ring (full/empty mbarriers);
+//       warp 1         -- allocates tensor memory; lane 0 issues tcgen05.mma
+//                         (kind::f16 or kind::i8, M=128, N=kBN) into a
+//                         double-buffered TMEM accumulator and releases ring
+//                         slots with tcgen05.commit;
+//       warps 2..5     -- epilogue: tcgen05.ld TMEM -> registers -> global C,
+//                         overlapping the mainloop of the next tile;
+//   * every mbarrier wait is bounded: on expiry the kernel records a failure
+//     word, drains its own copies in flight, frees TMEM and returns.
+//
+// One CTA computes a 128 x kBN tile of C; one ring stage holds 128 bytes of K
+// (64 fp16 or 128 int8 values) for A (128 rows) and B (kBN rows/cols).
+#pragma once
+
+#include <cuda_fp16.h>
+#include "tcg_ptx.cuh"
+
+namespace tcg {
+
+constexpr int kBM = 128;        // UMMA M (one CTA, cta_group::1)
+constexpr int kBKBytes = 128;   // bytes of K per ring stage (one swizzle row)
+constexpr int kThreads = 192;   // 6 warps
+constexpr int kGroupM = 16;     // tile-rows per rasterisation band
+
+constexpr uint32_t kErrWaitTimeout = 1;  // failure code in the high word
+
+// Failure word, one per device.  This header is compiled into exactly one
+// translation unit (tcgemm.cu), which owns the definition.
+__device__ unsigned long long g_tcg_error_word = 0ull;
+
+struct GemmParams {
+    void* C;
+    long long batch_stride_c;  // elements
+    int M, N, K, batches;
+    int tiles_m, tiles_n, num_kb;
+    int vec_store;             // C rows 16-byte aligned (N % 4 == 0, C aligned)
+    unsigned long long timeout_ns;
+};
+
+template <bool kI8, bool kAccF16, bool kBMn, int kBN, int kStages>
+struct GemmTraits {
+    static constexpr int kElem = kI8 ? 1 : 2;
+    static constexpr int kBK = kBKBytes / kElem;      // K elements per stage
+    static constexpr int kUmmaK = 32 / kElem;         // K per instruction (32 bytes)
+    static constexpr int kKSteps = kBK / kUmmaK;      // instructions per stage
+    static constexpr int kABytes = kBM * kBKBytes;
+    static constexpr int kBBytes = kBN * kBKBytes;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kTmemCols = 2 * kBN;         // two accumulators
+    // MN-major B arrives as kBN/kAtomN boxes of kAtomN (128 bytes) x kBK rows.
+    static constexpr int kAtomN = kBKBytes / kElem;
+    static constexpr int kBoxBytesMn = kBK * kBKBytes;
+    static constexpr uint32_t kIdesc =
+        make_idesc(kI8 ? 2u : (kAccF16 ? 0u : 1u), kI8 ? 1u : 0u, kBMn, kBM, kBN);
+    static constexpr int kBarrierBytes = 256;
+    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
+    static_assert(kBN % kAtomN == 0 || !kBMn, "MN-major B needs whole 128-byte atoms");
+    static_assert(kTmemCols >= 32 && kTmemCols <= 512, "TMEM allocation");
+    static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& b, int& tm, int& tn)
+{
+    const int per_batch = tiles_m * tiles_n;
+    b = t / per_batch;
+    const int r = t - b * per_batch;
+    const int band = kGroupM * tiles_n;
+    const int g = r / band;
+    const int first_m = g * kGroupM;
+    const int gsz = min(tiles_m - first_m, kGroupM);
+    const int rr = r - g * band;
+    tm = first_m + rr % gsz;
+    tn = rr / gsz;
+}
+
+__device__ __forceinline__ void record_failure(volatile uint32_t* abort_flag, uint32_t detail)
+{
+    *abort_flag = 1u;
+    __threadfence_block();
+    atomicCAS(&g_tcg_error_word, 0ull,
+              (static_cast<unsigned long long>(kErrWaitTimeout) << 32) | detail);
+}
+
+// Single-thread bounded wait.  true: the phase of `parity` completed.
+// false: this CTA is aborting (this wait expired, or another role's did).
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                             unsigned long long timeout_ns, uint32_t detail)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (global_timer_ns() - t0 > timeout_ns) {
+            record_failure(abort_flag, detail);
+            return false;
+        }
+    }
+}
+
+// Whole-warp bounded wait with a warp-uniform result.  A completed phase is
+// sticky until every waiter has arrived for the next one, so once any lane
+// sees completion all lanes will.
+__device__ __forceinline__ bool wait_bounded_warp(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                                  unsigned long long timeout_ns, uint32_t detail)
+{
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; ++i) {
+        const bool ok = mbar_try_wait(bar, parity);
+        if (__all_sync(0xffffffffu, ok)) return true;
+        if (__any_sync(0xffffffffu, ok)) continue;
+        if (i == 0) t0 = global_timer_ns();
+        const bool ab = (*abort_flag != 0u);
+        const bool expired = (global_timer_ns() - t0) > timeout_ns;
+        const unsigned stop = __ballot_sync(0xffffffffu, ab || expired);
+        if (stop) {
+            if ((threadIdx.x & 31) == (__ffs(stop) - 1) && !ab) record_failure(abort_flag, detail);
+            return false;
+        }
+    }
+}
+
+// Bounded drain wait used only on the abort path (ignores the abort flag).
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity)
+{
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (global_timer_ns() - t0 > 200000000ull) return;  // 200 ms
+    }
+}
+
+template <bool kI8, bool kAccF16, bool kBMn, int kBN, int kStages>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const GemmParams p)
+{
+    using T = GemmTraits<kI8, kAccF16, kBMn, kBN, kStages>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * T::kStageBytes);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + kStages;
+    uint64_t* tfull = bars + 2 * kStages;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(smem_u32(&tfull[a]), 1);
+            mbar_init(smem_u32(&tempty[a]), 4 * 32);
+        }
+        mbar_init(smem_u32(drain), 1);
+        *abort_flag = 0u;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), T::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int num_tiles = p.tiles_m * p.tiles_n * p.batches;
+    const uint32_t stage0 = smem_u32(smem);
+    // producer bookkeeping for the abort drain: per stage, a load was issued /
+    // the parity of its phase
+    uint32_t issued = 0, issued_parity = 0;
+
+    if (threadIdx.x == 0) {
+        // ------------------------------------------------ TMA producer ----
+        int stage = 0;
+        uint32_t phase = 0;
+        bool aborted = false;
+        for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x) {
+            int b, tm, tn;
+            tile_coords(t, p.tiles_m, p.tiles_n, b, tm, tn);
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                const uint32_t fb = smem_u32(&full[stage]);
+                if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.timeout_ns,
+                                  (blockIdx.x << 8) | 0x10u | stage)) {
+                    aborted = true;
+                    break;
+                }
+                mbar_arrive_expect_tx(fb, T::kStageBytes);
+                const uint32_t a_dst = stage0 + stage * T::kStageBytes;
+                const uint32_t b_dst = a_dst + T::kABytes;
+                tma_load_3d(a_dst, &tmA, fb, kb * T::kBK, tm * kBM, b);
+                if constexpr (kBMn) {
+#pragma unroll
+                    for (int j = 0; j < kBN / T::kAtomN; ++j)
+                        tma_load_3d(b_dst + j * T::kBoxBytesMn, &tmB, fb, tn * kBN + j * T::kAtomN,
+                                    kb * T::kBK, b);
+                } else {
+                    tma_load_3d(b_dst, &tmB, fb, kb * T::kBK, tn * kBN, b);
+                }
+                issued |= 1u << stage;
+                issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                if (++stage == kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+    } else if (threadIdx.x == 32) {
+        // -------------------------------------------------- MMA issuer ----
+        int stage = 0;
+        uint32_t phase = 0;
+        bool aborted = false;
+        int local = 0;
+        for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++local) {
+            const int acc = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            if (!wait_bounded(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, p.timeout_ns,
+                              (blockIdx.x << 8) | 0x20u | acc)) {
+                aborted = true;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                if (!wait_bounded(smem_u32(&full[stage]), phase, abort_flag, p.timeout_ns,
+                                  (blockIdx.x << 8) | 0x30u | stage)) {
+                    aborted = true;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_addr = stage0 + stage * T::kStageBytes;
+                const uint32_t b_addr = a_addr + T::kABytes;
+#pragma unroll
+                for (int k = 0; k < T::kKSteps; ++k) {
+                    const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
+                    const uint64_t bdesc =
+                        kBMn ? smem_desc_sw128(b_addr + k * T::kUmmaK * kBKBytes, T::kBoxBytesMn, 1024)
+                             : smem_desc_sw128(b_addr + k * 32, 16, 1024);
+                    umma<kI8>(d_tmem, adesc, bdesc, T::kIdesc, (kb | k) != 0 ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&empty[stage]));
+                if (++stage == kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!aborted) umma_commit(smem_u32(&tfull[acc]));
+        }
+    } else if (warp >= 2) {
+        // ---------------------------------------------------- epilogue ----
+        const int quarter = warp & 3;  // TMEM lanes this warp may read
+        uint32_t* Cbits = static_cast<uint32_t*>(p.C);
+        int local = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+            const int acc = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            if (!wait_bounded_warp(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.timeout_ns,
+                                   (blockIdx.x << 8) | 0x40u | acc))
+                break;
+            tc_fence_after();
+            int b, tm, tn;
+            tile_coords(t, p.tiles_m, p.tiles_n, b, tm, tn);
+            const int row = tm * kBM + quarter * 32 + lane;
+            const int col0 = tn * kBN;
+            uint32_t* crow = Cbits + static_cast<long long>(b) * p.batch_stride_c +
+                             static_cast<long long>(row) * p.N;
+            const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                    static_cast<uint32_t>(acc * kBN);
+#pragma unroll 1
+            for (int c = 0; c < kBN; c += 32) {
+                const int col = col0 + c;
+                if (col >= p.N) break;  // warp-uniform
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(t_addr + c, v);
+                tmem_ld_wait();
+                if constexpr (kAccF16) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        v[j] = __float_as_uint(__half2float(__ushort_as_half(static_cast<unsigned short>(v[j] & 0xFFFFu))));
+                }
+                if (row < p.M) {
+                    if (p.vec_store && col + 32 <= p.N) {
+                        uint4* dst = reinterpret_cast<uint4*>(crow + col);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            dst[j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col + j < p.N) crow[col + j] = v[j];
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(smem_u32(&tempty[acc]));
+        }
+    }
+
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (*abort_flag) {
+        // Some role gave up.  Before shared and tensor memory are released,
+        // let this CTA's own TMA copies land and its MMAs retire.
+        if (threadIdx.x == 0) {
+            for (int s = 0; s < kStages; ++s)
+                if (issued & (1u << s)) drain_wait(smem_u32(&full[s]), (issued_parity >> s) & 1u);
+        } else if (threadIdx.x == 32) {
+            umma_commit(smem_u32(drain));
+            drain_wait(smem_u32(drain), 0);
+        }
+        __syncwarp();
+        __syncthreads();
+    }
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, T::kTmemCols);
+}
+
+// Widen packed int4 (two per byte, low nibble first) to int8, 16 packed bytes
+// per thread per step.
+__device__ __forceinline__ void widen_word(uint32_t w, uint32_t& o0, uint32_t& o1)
+{
+    uint32_t lo = w & 0x0F0F0F0Fu;
+    uint32_t hi = (w >> 4) & 0x0F0F0F0Fu;
+    lo = __vsub4(lo ^ 0x08080808u, 0x08080808u);  // sign-extend each nibble
+    hi = __vsub4(hi ^ 0x08080808u, 0x08080808u);
+    o0 = __byte_perm(lo, hi, 0x5140);  // lo0 hi0 lo1 hi1
+    o1 = __byte_perm(lo, hi, 0x7362);  // lo2 hi2 lo3 hi3
+}
+
+__global__ void unpack_s4_kernel(const uint4* __restrict__ in, uint4* __restrict__ out, long long n16,
+                                 const int8_t* __restrict__ tail_in, int8_t* __restrict__ tail_out,
+                                 int tail)
+{
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16; i += stride) {
+        const uint4 v = in[i];
+        uint4 a, b;
+        widen_word(v.x, a.x, a.y);
+        widen_word(v.y, a.z, a.w);
+        widen_word(v.z, b.x, b.y);
+        widen_word(v.w, b.z, b.w);
+        out[2 * i] = a;
+        out[2 * i + 1] = b;
+    }
+    if (blockIdx.x == 0 && threadIdx.x < tail) {
+        const int8_t x = tail_in[threadIdx.x];
+        tail_out[2 * threadIdx.x] = static_cast<int8_t>(static_cast<int8_t>(x << 4) >> 4);
+        tail_out[2 * threadIdx.x + 1] = static_cast<int8_t>(x >> 4);
+    }
+}
+
+}  // namespace tcg

