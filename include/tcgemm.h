@@ -80,6 +80,33 @@ tcg_status tcg_gemm_s4(const int8_t* A_packed, const int8_t* BT_packed, int32_t*
  * The first stage of tcg_gemm_s4, exposed for reuse. */
 tcg_status tcg_unpack_s4(const int8_t* packed, int8_t* out, size_t n_packed, void* stream);
 
+/* No counterpart in the reference.  tcg_gemm_s4 without allocation.
+ *
+ * Some callers cannot allocate device memory at all: a host application or
+ * serving framework that owns the whole device-memory budget and forbids its
+ * plugins to allocate, or a latency-critical path that cannot accept the
+ * device-wide synchronisation cudaMalloc implies, or code written to the
+ * reference's int4 `launch_kernel` contract, which takes no workspace and
+ * allocates nothing.  tcg_gemm_s4 needs scratch for the widened operands, so
+ * for those callers this variant keeps it in one fixed device array inside
+ * libtcgemm.so, TCG_S4_STATIC_SCRATCH_BYTES large, that every GPU which loads
+ * the library holds until the process exits.
+ *
+ * Same operands, result and status codes as tcg_gemm_s4.  The scratch need
+ * (tcg_gemm_s4_workspace_size(M, N, K, batches)) must not exceed
+ * TCG_S4_STATIC_SCRATCH_BYTES: larger problems return TCG_ERR_WORKSPACE and
+ * launch nothing (4096 x 4096 x 4096 fits exactly).  No cudaMalloc/cudaFree
+ * or other allocating routine is called.  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture.  All calls share
+ * the one array: calls that overlap on the GPU (other streams, other host
+ * threads) race on it and must be serialised by the caller.  The array keeps
+ * the last call's contents; every call overwrites all of the scratch it reads,
+ * so nothing has to start at zero. */
+#define TCG_S4_STATIC_SCRATCH_BYTES (32u << 20)
+tcg_status tcg_gemm_s4_static(const int8_t* A_packed, const int8_t* BT_packed, int32_t* C,
+                              int M, int N, int K, int batches, void* stream);
+
 /* Device-side failure word.  Every wait inside the GEMM kernel is bounded
  * (default 2 s, tcg_set_wait_timeout_ns); on expiry the kernel records
  * (code << 32 | detail) here, drains its own copies in flight, frees its

@@ -30,6 +30,7 @@ SIGNATURES = {
     "tcg_gemm_s4_workspace_size": (_sz, [_i, _i, _i, _i]),
     "tcg_gemm_s4": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _p, _sz, _p]),
     "tcg_unpack_s4": (C.c_int, [_p, _p, _sz, _p]),
+    "tcg_gemm_s4_static": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _p]),
     "tcg_check_device_error": (C.c_int, [_p, C.POINTER(C.c_uint64)]),
     "tcg_set_wait_timeout_ns": (None, [C.c_uint64]),
     "tcg_set_tile_n": (None, [_i]),

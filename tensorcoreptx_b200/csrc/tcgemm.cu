@@ -323,6 +323,58 @@ tcg_status tcg_gemm_s4(const int8_t* A_packed, const int8_t* BT_packed, int32_t*
     return s;
 }
 
+}  // extern "C"
+
+// ---- int4 GEMM without allocation: scratch in a fixed device array -------
+//
+// For callers that may not allocate device memory (see tcgemm.h).  Host code
+// must never pass `g_s4_static_scratch` itself to a kernel: on the host that
+// name is only a stand-in for the symbol, not a device address.  The device
+// address is looked up once per device with cudaGetSymbolAddress.
+namespace {
+
+static __device__ __align__(256) unsigned char g_s4_static_scratch[TCG_S4_STATIC_SCRATCH_BYTES];
+
+struct StaticScratch {
+    std::once_flag once;
+    cudaError_t err = cudaSuccess;
+    void* ptr = nullptr;
+};
+StaticScratch g_s4_static[kMaxDevices];
+
+// Device address of the array on the current device; the lookup runs on the
+// first call per device, with that device current.
+tcg_status static_scratch(void** out)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev < 0 || dev >= kMaxDevices) return TCG_ERR_UNSUPPORTED;
+    StaticScratch& s = g_s4_static[dev];
+    std::call_once(s.once, [&]() { s.err = cudaGetSymbolAddress(&s.ptr, g_s4_static_scratch); });
+    if (s.err != cudaSuccess || s.ptr == nullptr) return cuda_fail(s.err != cudaSuccess ? s.err : cudaErrorInvalidSymbol);
+    *out = s.ptr;
+    return TCG_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" {
+
+tcg_status tcg_gemm_s4_static(const int8_t* A_packed, const int8_t* BT_packed, int32_t* C, int M, int N, int K,
+                              int batches, void* stream)
+{
+    if (M < 0 || N < 0 || K < 0 || batches < 0) return TCG_ERR_SHAPE;
+    if (tcg_gemm_s4_workspace_size(M, N, K, batches) > TCG_S4_STATIC_SCRATCH_BYTES) return TCG_ERR_WORKSPACE;
+    DeviceState* dev;
+    tcg_status s = device_state(&dev);
+    if (s != TCG_SUCCESS) return s;
+    void* ws = nullptr;
+    if ((s = static_scratch(&ws)) != TCG_SUCCESS) return s;
+    // the caller-workspace path of tcg_gemm_s4: it allocates nothing
+    return tcg_gemm_s4(A_packed, BT_packed, C, M, N, K, batches, ws, TCG_S4_STATIC_SCRATCH_BYTES, stream);
+}
+
 tcg_status tcg_unpack_s4(const int8_t* packed, int8_t* out, size_t n_packed, void* stream)
 {
     if (n_packed == 0) return TCG_SUCCESS;
