@@ -116,15 +116,21 @@ tcg_status tcg_gemm_s4_static(const int8_t* A_packed, const int8_t* BT_packed, i
 tcg_status tcg_check_device_error(void* stream, uint64_t* word);
 void tcg_set_wait_timeout_ns(uint64_t ns);
 
-/* Tile width override for tuning (0 = automatic; else 64, 128 or 256). */
+/* Tile overrides for tuning: the tile width (0 = automatic; else 64, 128 or
+ * 256) and the CTA shape (0 = automatic, 1 = single-CTA 128-row tiles,
+ * 2 = two-CTA 256-row tiles).  Shapes a precision cannot run fall back to
+ * the nearest valid one. */
 void tcg_set_tile_n(int bn);
+void tcg_set_cta_pair(int mode);
 
 /* Introspection: last CUDA error code seen, status names, library version,
- * and the tile width chosen by the most recent launch on this thread. */
+ * and the tile shape (width, rows) chosen by the most recent launch on this
+ * thread. */
 int tcg_last_cuda_error(void);
 const char* tcg_status_string(tcg_status s);
 int tcg_version(void);
 int tcg_last_tile_n(void);
+int tcg_last_tile_m(void);
 
 #ifdef __cplusplus
 }

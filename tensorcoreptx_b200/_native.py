@@ -34,10 +34,12 @@ SIGNATURES = {
     "tcg_check_device_error": (C.c_int, [_p, C.POINTER(C.c_uint64)]),
     "tcg_set_wait_timeout_ns": (None, [C.c_uint64]),
     "tcg_set_tile_n": (None, [_i]),
+    "tcg_set_cta_pair": (None, [_i]),
     "tcg_last_cuda_error": (C.c_int, []),
     "tcg_status_string": (C.c_char_p, [_i]),
     "tcg_version": (C.c_int, []),
     "tcg_last_tile_n": (C.c_int, []),
+    "tcg_last_tile_m": (C.c_int, []),
 }
 
 _lib = None

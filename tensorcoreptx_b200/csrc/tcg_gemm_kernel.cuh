@@ -47,26 +47,31 @@ struct GemmParams {
     unsigned long long timeout_ns;
 };
 
-template <bool kI8, bool kAccF16, bool kBMn, int kBN, int kStages>
+template <bool kI8, bool kAccF16, bool kBMn, int kBN, int kStages, bool kPair>
 struct GemmTraits {
     static constexpr int kElem = kI8 ? 1 : 2;
     static constexpr int kBK = kBKBytes / kElem;      // K elements per stage
     static constexpr int kUmmaK = 32 / kElem;         // K per instruction (32 bytes)
     static constexpr int kKSteps = kBK / kUmmaK;      // instructions per stage
+    static constexpr int kTileM = kPair ? 2 * kBM : kBM;  // rows of C per tile
+    static constexpr int kBRows = kPair ? kBN / 2 : kBN;  // B rows (N) held by each CTA
     static constexpr int kABytes = kBM * kBKBytes;
-    static constexpr int kBBytes = kBN * kBKBytes;
-    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kBBytes = kBRows * kBKBytes;
+    static constexpr int kStageBytes = kABytes + kBBytes;       // per CTA
+    static constexpr int kTxBytes = kPair ? 2 * kStageBytes : kStageBytes;  // per leader barrier
     static constexpr int kTmemCols = 2 * kBN;         // two accumulators
-    // MN-major B arrives as kBN/kAtomN boxes of kAtomN (128 bytes) x kBK rows.
+    // MN-major B arrives as kBRows/kAtomN boxes of kAtomN (128 bytes) x kBK rows.
     static constexpr int kAtomN = kBKBytes / kElem;
     static constexpr int kBoxBytesMn = kBK * kBKBytes;
     static constexpr uint32_t kIdesc =
-        make_idesc(kI8 ? 2u : (kAccF16 ? 0u : 1u), kI8 ? 1u : 0u, kBMn, kBM, kBN);
+        make_idesc(kI8 ? 2u : (kAccF16 ? 0u : 1u), kI8 ? 1u : 0u, kBMn, kTileM, kBN);
+    static constexpr int kEpiArrivals = kPair ? 8 : 4;  // one per epilogue warp (of both CTAs)
     static constexpr int kBarrierBytes = 256;
     static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
-    static_assert(kBN % kAtomN == 0 || !kBMn, "MN-major B needs whole 128-byte atoms");
+    static_assert(kBRows % kAtomN == 0 || !kBMn, "MN-major B needs whole 128-byte atoms");
     static_assert(kTmemCols >= 32 && kTmemCols <= 512, "TMEM allocation");
     static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+    static_assert(2 * kStages + 5 <= 30, "barrier area");
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& b, int& tm, int& tn)
@@ -139,12 +144,34 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity)
     }
 }
 
-template <bool kI8, bool kAccF16, bool kBMn, int kBN, int kStages>
+__device__ __forceinline__ uint32_t cluster_id_x()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t num_clusters_x()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+
+// kPair = false: one CTA per 128 x kBN tile, tcgen05 cta_group::1.
+// kPair = true : a cluster of two CTAs per 256 x kBN tile, tcgen05
+//   cta_group::2.  CTA r holds rows [128r, 128r+128) of A and columns
+//   [r*kBN/2, (r+1)*kBN/2) of B; the leader (rank 0) issues every MMA, which
+//   reads both CTAs' shared memory and writes rows 128r.. of D into CTA r's
+//   tensor memory.  Both CTAs' TMA loads complete on the leader's full
+//   barriers; the leader's commits arrive on both CTAs' empty / tmem-full
+//   barriers; both epilogues release the accumulator on the leader's barrier.
+template <bool kI8, bool kAccF16, bool kBMn, int kBN, int kStages, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const GemmParams p)
 {
-    using T = GemmTraits<kI8, kAccF16, kBMn, kBN, kStages>;
+    using T = GemmTraits<kI8, kAccF16, kBMn, kBN, kStages, kPair>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -159,6 +186,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+    const bool leader = (rank == 0u);
+    const int unit = kPair ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
+    const int units = kPair ? static_cast<int>(num_clusters_x()) : static_cast<int>(gridDim.x);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -167,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(smem_u32(&tfull[a]), 1);
-            mbar_init(smem_u32(&tempty[a]), 4 * 32);
+            mbar_init(smem_u32(&tempty[a]), T::kEpiArrivals);
         }
         mbar_init(smem_u32(drain), 1);
         *abort_flag = 0u;
@@ -176,11 +207,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&tmB);
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_slot), T::kTmemCols);
-        tmem_relinquish();
+        if constexpr (kPair) {
+            tmem_alloc_pair(smem_u32(tmem_slot), T::kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_slot), T::kTmemCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (kPair) cluster_sync_all();  // the peer's barriers exist before any remote arrival
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -195,27 +232,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         int stage = 0;
         uint32_t phase = 0;
         bool aborted = false;
-        for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x) {
+        for (int t = unit; t < num_tiles && !aborted; t += units) {
             int b, tm, tn;
             tile_coords(t, p.tiles_m, p.tiles_n, b, tm, tn);
+            const int a_row = tm * T::kTileM + static_cast<int>(rank) * kBM;
+            const int b_row = tn * kBN + static_cast<int>(rank) * T::kBRows;
             for (int kb = 0; kb < p.num_kb; ++kb) {
-                const uint32_t fb = smem_u32(&full[stage]);
+                const uint32_t fb_local = smem_u32(&full[stage]);
                 if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.timeout_ns,
                                   (blockIdx.x << 8) | 0x10u | stage)) {
                     aborted = true;
                     break;
                 }
-                mbar_arrive_expect_tx(fb, T::kStageBytes);
                 const uint32_t a_dst = stage0 + stage * T::kStageBytes;
                 const uint32_t b_dst = a_dst + T::kABytes;
-                tma_load_3d(a_dst, &tmA, fb, kb * T::kBK, tm * kBM, b);
-                if constexpr (kBMn) {
+                if constexpr (kPair) {
+                    const uint32_t fb = mapa_shared(fb_local, 0);  // the leader's full barrier
+                    if (leader) mbar_arrive_expect_tx(fb_local, T::kTxBytes);
+                    tma_load_3d_pair(a_dst, &tmA, fb, kb * T::kBK, a_row, b);
+                    if constexpr (kBMn) {
 #pragma unroll
-                    for (int j = 0; j < kBN / T::kAtomN; ++j)
-                        tma_load_3d(b_dst + j * T::kBoxBytesMn, &tmB, fb, tn * kBN + j * T::kAtomN,
-                                    kb * T::kBK, b);
+                        for (int j = 0; j < T::kBRows / T::kAtomN; ++j)
+                            tma_load_3d_pair(b_dst + j * T::kBoxBytesMn, &tmB, fb, b_row + j * T::kAtomN,
+                                             kb * T::kBK, b);
+                    } else {
+                        tma_load_3d_pair(b_dst, &tmB, fb, kb * T::kBK, b_row, b);
+                    }
                 } else {
-                    tma_load_3d(b_dst, &tmB, fb, kb * T::kBK, tn * kBN, b);
+                    mbar_arrive_expect_tx(fb_local, T::kTxBytes);
+                    tma_load_3d(a_dst, &tmA, fb_local, kb * T::kBK, a_row, b);
+                    if constexpr (kBMn) {
+#pragma unroll
+                        for (int j = 0; j < T::kBRows / T::kAtomN; ++j)
+                            tma_load_3d(b_dst + j * T::kBoxBytesMn, &tmB, fb_local, b_row + j * T::kAtomN,
+                                        kb * T::kBK, b);
+                    } else {
+                        tma_load_3d(b_dst, &tmB, fb_local, kb * T::kBK, b_row, b);
+                    }
                 }
                 issued |= 1u << stage;
                 issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -225,13 +278,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-    } else if (threadIdx.x == 32) {
+        // Tail: wait until every stage this CTA filled has been released, so
+        // no MMA commit arrives on this CTA's barriers after it exits.
+        for (int i = 0; i < kStages && !aborted; ++i) {
+            if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.timeout_ns,
+                              (blockIdx.x << 8) | 0x50u | stage))
+                break;
+            if (++stage == kStages) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+    } else if (threadIdx.x == 32 && leader) {
         // -------------------------------------------------- MMA issuer ----
         int stage = 0;
         uint32_t phase = 0;
         bool aborted = false;
         int local = 0;
-        for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++local) {
+        for (int t = unit; t < num_tiles && !aborted; t += units, ++local) {
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
             if (!wait_bounded(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, p.timeout_ns,
@@ -256,22 +320,41 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint64_t bdesc =
                         kBMn ? smem_desc_sw128(b_addr + k * T::kUmmaK * kBKBytes, T::kBoxBytesMn, 1024)
                              : smem_desc_sw128(b_addr + k * 32, 16, 1024);
-                    umma<kI8>(d_tmem, adesc, bdesc, T::kIdesc, (kb | k) != 0 ? 1u : 0u);
+                    if constexpr (kPair)
+                        umma_pair<kI8>(d_tmem, adesc, bdesc, T::kIdesc, (kb | k) != 0 ? 1u : 0u);
+                    else
+                        umma<kI8>(d_tmem, adesc, bdesc, T::kIdesc, (kb | k) != 0 ? 1u : 0u);
                 }
-                umma_commit(smem_u32(&empty[stage]));
+                if constexpr (kPair)
+                    umma_commit_pair(smem_u32(&empty[stage]), 0x3);
+                else
+                    umma_commit(smem_u32(&empty[stage]));
                 if (++stage == kStages) {
                     stage = 0;
                     phase ^= 1u;
                 }
             }
-            if (!aborted) umma_commit(smem_u32(&tfull[acc]));
+            if (!aborted) {
+                if constexpr (kPair)
+                    umma_commit_pair(smem_u32(&tfull[acc]), 0x3);
+                else
+                    umma_commit(smem_u32(&tfull[acc]));
+            }
+        }
+        // Tail: wait until both accumulators' last use has been released by
+        // the epilogue(s), so no release arrives on this CTA after it exits.
+        for (int i = 0; i < 2 && !aborted; ++i, ++local) {
+            if (!wait_bounded(smem_u32(&tempty[local & 1]), ((local >> 1) & 1) ^ 1u, abort_flag, p.timeout_ns,
+                              (blockIdx.x << 8) | 0x60u | (local & 1)))
+                break;
         }
     } else if (warp >= 2) {
         // ---------------------------------------------------- epilogue ----
         const int quarter = warp & 3;  // TMEM lanes this warp may read
         uint32_t* Cbits = static_cast<uint32_t*>(p.C);
+        const uint32_t tempty_leader0 = kPair ? mapa_shared(smem_u32(&tempty[0]), 0) : smem_u32(&tempty[0]);
         int local = 0;
-        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+        for (int t = unit; t < num_tiles; t += units, ++local) {
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
             if (!wait_bounded_warp(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.timeout_ns,
@@ -280,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             int b, tm, tn;
             tile_coords(t, p.tiles_m, p.tiles_n, b, tm, tn);
-            const int row = tm * kBM + quarter * 32 + lane;
+            const int row = tm * T::kTileM + static_cast<int>(rank) * kBM + quarter * 32 + lane;
             const int col0 = tn * kBN;
             uint32_t* crow = Cbits + static_cast<long long>(b) * p.batch_stride_c +
                              static_cast<long long>(row) * p.N;
@@ -312,7 +395,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             tc_fence_before();
-            mbar_arrive(smem_u32(&tempty[acc]));
+            __syncwarp();
+            if (lane == 0) {
+                const uint32_t tb = tempty_leader0 + static_cast<uint32_t>(acc * sizeof(uint64_t));
+                if constexpr (kPair)
+                    mbar_arrive_cluster(tb);
+                else
+                    mbar_arrive(tb);
+            }
         }
     }
 
@@ -322,18 +412,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (*abort_flag) {
         // Some role gave up.  Before shared and tensor memory are released,
         // let this CTA's own TMA copies land and its MMAs retire.
-        if (threadIdx.x == 0) {
-            for (int s = 0; s < kStages; ++s)
-                if (issued & (1u << s)) drain_wait(smem_u32(&full[s]), (issued_parity >> s) & 1u);
-        } else if (threadIdx.x == 32) {
-            umma_commit(smem_u32(drain));
+        if (threadIdx.x == 0 && issued) {
+            if (!kPair || leader) {
+                for (int s = 0; s < kStages; ++s)
+                    if (issued & (1u << s)) drain_wait(smem_u32(&full[s]), (issued_parity >> s) & 1u);
+            } else {
+                // the peer's copies complete on the leader's barriers: give
+                // them a fixed 2 ms, far above a copy's latency
+                const uint64_t t0 = global_timer_ns();
+                while (global_timer_ns() - t0 < 2000000ull) {
+                }
+            }
+        } else if (threadIdx.x == 32 && leader) {
+            if constexpr (kPair)
+                umma_commit_pair_local(smem_u32(drain));
+            else
+                umma_commit(smem_u32(drain));
             drain_wait(smem_u32(drain), 0);
         }
         __syncwarp();
         __syncthreads();
     }
+    if constexpr (kPair) cluster_sync_all();  // neither CTA frees TMEM / exits before the other is done
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem_base, T::kTmemCols);
+    if (warp == 1) {
+        if constexpr (kPair)
+            tmem_dealloc_pair(tmem_base, T::kTmemCols);
+        else
+            tmem_dealloc(tmem_base, T::kTmemCols);
+    }
 }
 
 // Widen packed int4 (two per byte, low nibble first) to int8, 16 packed bytes

@@ -24,8 +24,10 @@ constexpr int kMaxDevices = 64;
 
 thread_local int t_last_cuda_error = 0;
 thread_local int t_last_tile_n = 0;
+thread_local int t_last_tile_m = 0;
 std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
 std::atomic<int> g_force_bn{0};
+std::atomic<int> g_force_pair{0};
 
 struct DeviceState {
     std::once_flag once;
@@ -98,35 +100,51 @@ tcg_status encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
     return TCG_SUCCESS;
 }
 
-// Tile width: minimise (waves of persistent CTAs) x (tile width), i.e. the
-// critical path in units of one 128-column tile, preferring wider tiles (less
-// L2 traffic per MAC) unless a narrower one saves more than 3 %.
-int choose_bn(int M, int N, int batches, int sms)
+// Tile shape.  Candidates: single-CTA 128 x BN tiles (BN in 64/128/256, one
+// per SM) and CTA-pair 256 x BN tiles (BN in 128/256, one pair per two SMs).
+// Cost = waves of persistent units x BN: the critical path in units of one
+// SM's 128-column share of a tile.  Pairs read a third less operand data per
+// MAC from L2 than single 128 x 256 tiles, so they win ties; a narrower or
+// single-CTA shape must save more than 3 % to be chosen.
+struct TileChoice {
+    int bn;
+    bool pair;
+};
+
+TileChoice choose_tile(int M, int N, int batches, int sms, bool i8_mn)
 {
-    const int forced = g_force_bn.load();
-    if (forced == 64 || forced == 128 || forced == 256) return forced;
-    const long long tm = (M + kBM - 1) / kBM;
-    int best = 256;
-    double best_cost = 0;
-    for (int bn : {256, 128, 64}) {
-        const long long tiles = tm * ((N + bn - 1) / bn) * batches;
-        const long long waves = (tiles + sms - 1) / sms;
-        const double cost = static_cast<double>(waves) * bn;
-        if (bn == 256 || cost < best_cost * 0.97) {
-            best = bn;
-            best_cost = cost;
+    const int forced_bn = g_force_bn.load();
+    const int forced_pair = g_force_pair.load();  // 0 auto, 1 single, 2 pair
+    TileChoice best{256, true};
+    double best_cost = -1.0;
+    for (int pair = 1; pair >= 0; --pair) {
+        if ((forced_pair == 1 && pair) || (forced_pair == 2 && !pair)) continue;
+        for (int bn : {256, 128, 64}) {
+            if (pair && bn == 64) continue;
+            if (i8_mn && (pair ? bn / 2 : bn) < 128) continue;  // whole 128-byte atoms
+            if (forced_bn && bn != forced_bn) continue;
+            const long long tm = (M + (pair ? 255 : 127)) / (pair ? 256 : 128);
+            const long long tiles = tm * ((N + bn - 1) / bn) * batches;
+            const long long units = pair ? sms / 2 : sms;
+            const long long waves = (tiles + units - 1) / units;
+            const double cost = static_cast<double>(waves) * bn;
+            if (best_cost < 0 || cost < best_cost * 0.97) {
+                best = TileChoice{bn, pair != 0};
+                best_cost = cost;
+            }
         }
     }
+    if (best_cost < 0) best = TileChoice{forced_bn ? forced_bn : 256, forced_pair != 1};
     return best;
 }
 
-template <bool kI8, bool kAccF16, bool kBMn, int kBN>
+template <bool kI8, bool kAccF16, bool kBMn, int kBN, bool kPair>
 tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, int M, int N, int K,
                        int batches, cudaStream_t st)
 {
-    constexpr int kStages = kBN == 256 ? 4 : (kBN == 128 ? 6 : 8);
-    using T = GemmTraits<kI8, kAccF16, kBMn, kBN, kStages>;
-    auto kern = gemm_kernel<kI8, kAccF16, kBMn, kBN, kStages>;
+    constexpr int kStages = kPair ? (kBN == 256 ? 6 : 8) : (kBN == 256 ? 4 : (kBN == 128 ? 6 : 8));
+    using T = GemmTraits<kI8, kAccF16, kBMn, kBN, kStages, kPair>;
+    auto kern = gemm_kernel<kI8, kAccF16, kBMn, kBN, kStages, kPair>;
 
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e);
@@ -139,7 +157,7 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     if (kBMn)  // B is K x N, N contiguous
         s = encode_3d(&mB, dt, B, N, K, batches, N * es, static_cast<uint64_t>(K) * N * es, T::kAtomN, T::kBK);
     else  // B is N x K, K contiguous
-        s = encode_3d(&mB, dt, B, K, N, batches, K * es, static_cast<uint64_t>(N) * K * es, T::kBK, kBN);
+        s = encode_3d(&mB, dt, B, K, N, batches, K * es, static_cast<uint64_t>(N) * K * es, T::kBK, T::kBRows);
     if (s != TCG_SUCCESS) return s;
 
     GemmParams p;
@@ -149,7 +167,7 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     p.N = N;
     p.K = K;
     p.batches = batches;
-    p.tiles_m = (M + kBM - 1) / kBM;
+    p.tiles_m = (M + T::kTileM - 1) / T::kTileM;
     p.tiles_n = (N + kBN - 1) / kBN;
     p.num_kb = (K + T::kBK - 1) / T::kBK;
     p.vec_store = ((N % 4) == 0 && (reinterpret_cast<uintptr_t>(C) % 16) == 0) ? 1 : 0;
@@ -157,11 +175,45 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
 
     const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n * batches;
     if (tiles > 0x7fffffffLL) return TCG_ERR_SHAPE;
-    const int grid = static_cast<int>(tiles < dev.sms ? tiles : dev.sms);
-    kern<<<grid, kThreads, T::kSmemBytes, st>>>(mA, mB, p);
+    if constexpr (kPair) {
+        const long long pairs = dev.sms / 2;
+        cudaLaunchConfig_t cfg;
+        std::memset(&cfg, 0, sizeof cfg);
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * (tiles < pairs ? tiles : pairs)), 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = T::kSmemBytes;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        // persistent grid: no more pairs than can be resident at once
+        static int max_clusters[kMaxDevices] = {0};
+        int dev_id = 0;
+        cudaGetDevice(&dev_id);
+        if (max_clusters[dev_id] == 0) {
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+                cudaGetLastError();  // not fatal: fall back to one pair per two SMs
+                n = static_cast<int>(pairs);
+            }
+            max_clusters[dev_id] = n;
+        }
+        const long long units = max_clusters[dev_id] < pairs ? max_clusters[dev_id] : pairs;
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * (tiles < units ? tiles : units)), 1, 1);
+        e = cudaLaunchKernelEx(&cfg, kern, mA, mB, p);
+        if (e != cudaSuccess) return cuda_fail(e);
+    } else {
+        const int grid = static_cast<int>(tiles < dev.sms ? tiles : dev.sms);
+        kern<<<grid, kThreads, T::kSmemBytes, st>>>(mA, mB, p);
+    }
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
     t_last_tile_n = kBN;
+    t_last_tile_m = T::kTileM;
     return TCG_SUCCESS;
 }
 
@@ -169,15 +221,20 @@ template <bool kI8, bool kAccF16, bool kBMn>
 tcg_status dispatch_bn(DeviceState& dev, const void* A, const void* B, void* C, int M, int N, int K,
                        int batches, cudaStream_t st)
 {
-    int bn = choose_bn(M, N, batches, dev.sms);
-    // an MN-major int8 tile spans whole 128-byte swizzle atoms: 128 columns
-    if (kI8 && kBMn && bn == 64) bn = 128;
-    switch (bn) {
+    const TileChoice c = choose_tile(M, N, batches, dev.sms, kI8 && kBMn);
+    if (c.pair) {
+        if (c.bn == 128) {
+            // an MN-major int8 pair tile needs 128 columns per CTA
+            if constexpr (!(kI8 && kBMn)) return launch_gemm<kI8, kAccF16, kBMn, 128, true>(dev, A, B, C, M, N, K, batches, st);
+        }
+        return launch_gemm<kI8, kAccF16, kBMn, 256, true>(dev, A, B, C, M, N, K, batches, st);
+    }
+    switch (c.bn) {
     case 64:
-        if constexpr (!(kI8 && kBMn)) return launch_gemm<kI8, kAccF16, kBMn, 64>(dev, A, B, C, M, N, K, batches, st);
+        if constexpr (!(kI8 && kBMn)) return launch_gemm<kI8, kAccF16, kBMn, 64, false>(dev, A, B, C, M, N, K, batches, st);
         [[fallthrough]];
-    case 128: return launch_gemm<kI8, kAccF16, kBMn, 128>(dev, A, B, C, M, N, K, batches, st);
-    default: return launch_gemm<kI8, kAccF16, kBMn, 256>(dev, A, B, C, M, N, K, batches, st);
+    case 128: return launch_gemm<kI8, kAccF16, kBMn, 128, false>(dev, A, B, C, M, N, K, batches, st);
+    default: return launch_gemm<kI8, kAccF16, kBMn, 256, false>(dev, A, B, C, M, N, K, batches, st);
     }
 }
 
@@ -405,6 +462,8 @@ void tcg_set_wait_timeout_ns(uint64_t ns) { g_timeout_ns.store(ns ? ns : 2000000
 void tcg_set_tile_n(int bn) { g_force_bn.store(bn); }
 int tcg_last_cuda_error(void) { return t_last_cuda_error; }
 int tcg_last_tile_n(void) { return t_last_tile_n; }
+int tcg_last_tile_m(void) { return t_last_tile_m; }
+void tcg_set_cta_pair(int mode) { g_force_pair.store(mode); }
 int tcg_version(void) { return 100; }
 
 const char* tcg_status_string(tcg_status s)

@@ -169,5 +169,16 @@ def set_tile_n(bn: int) -> None:
     nat.lib().tcg_set_tile_n(int(bn))
 
 
+def set_cta_pair(mode: int) -> None:
+    """Force the CTA shape: 0 automatic, 1 single-CTA 128-row tiles, 2 two-CTA
+    (cta_group::2) 256-row tiles."""
+    nat.lib().tcg_set_cta_pair(int(mode))
+
+
 def last_tile_n() -> int:
     return int(nat.lib().tcg_last_tile_n())
+
+
+def last_tile_m() -> int:
+    """Rows of C per tile in the most recent launch: 128 (single CTA) or 256 (pair)."""
+    return int(nat.lib().tcg_last_tile_m())

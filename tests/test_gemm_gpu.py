@@ -388,3 +388,66 @@ def test_runs_on_current_stream():
     s.synchronize()
     ref = O.gemm_s8(A.cpu().numpy(), BT.cpu().numpy())
     assert np.array_equal(C.cpu().numpy(), ref)
+
+
+# ------------------------------------------------- tile shapes & CTA pairs --
+
+_SHAPE_CASES = [(1, 300, 520, 384), (2, 260, 136, 128), (1, 512, 1024, 256)]
+
+
+@pytest.mark.parametrize("prec", ["int8", "int8_kn", "int4", "fp16", "fp16_nk", "fp16acc"])
+def test_every_tile_shape_gives_identical_results(prec):
+    """Single-CTA 128-row tiles (widths 64/128/256) and CTA-pair 256-row tiles
+    (widths 128/256) must all produce the same C: integer results equal the
+    oracle, and fp16 results are bit-identical across shapes because every
+    element accumulates in the same k order."""
+    T = tcg()
+    for (bt, M, N, K) in _SHAPE_CASES:
+        rng = np.random.default_rng(bt * 1000 + M + N + K)
+        shp = (lambda r, c: (bt, r, c)) if bt > 1 else (lambda r, c: (r, c))
+        if prec.startswith("int8"):
+            A = rand_s8(rng, shp(M, K))
+            B = rand_s8(rng, shp(K, N) if prec == "int8_kn" else shp(N, K))
+            fn = (lambda: T.gemm_int8_kn(_cuda(A), _cuda(B))) if prec == "int8_kn" else \
+                 (lambda: T.gemm_int8(_cuda(A), _cuda(B)))
+        elif prec == "int4":
+            A = rand_s8(rng, shp(M, K // 2))
+            B = rand_s8(rng, shp(N, K // 2))
+            fn = lambda: T.gemm_int4(_cuda(A), _cuda(B))
+        else:
+            A = rand_f16_bits(rng, shp(M, K))
+            B = rand_f16_bits(rng, shp(N, K) if prec == "fp16_nk" else shp(K, N))
+            acc = "fp16" if prec == "fp16acc" else "fp32"
+            fn = (lambda: T.gemm_fp16_nk(_cuda(A, torch.float16), _cuda(B, torch.float16), acc=acc)) \
+                if prec == "fp16_nk" else \
+                (lambda: T.gemm_fp16(_cuda(A, torch.float16), _cuda(B, torch.float16), acc=acc))
+        outs = {}
+        try:
+            for mode, bns in ((1, (64, 128, 256)), (2, (128, 256))):
+                for bn in bns:
+                    T.set_cta_pair(mode)
+                    T.set_tile_n(bn)
+                    outs[(mode, bn)] = fn().cpu().numpy()
+                    shape_used = (T.last_tile_m(), T.last_tile_n())
+                    if not (prec == "int8_kn" and (mode, bn) in ((1, 64), (2, 128))):
+                        assert shape_used == (128 * mode, bn), (prec, mode, bn, shape_used)
+        finally:
+            T.set_cta_pair(0)
+            T.set_tile_n(0)
+        first = next(iter(outs.values()))
+        for key, out in outs.items():
+            assert np.array_equal(out.view(np.uint32), first.view(np.uint32)), (prec, key)
+        # and the common result is right
+        for b in range(bt):
+            out_b = first[b] if bt > 1 else first
+            Ab = A[b] if bt > 1 else A
+            Bb = B[b] if bt > 1 else B
+            if prec == "int8":
+                assert np.array_equal(out_b, O.gemm_s8(Ab, Bb, threads=8))
+            elif prec == "int8_kn":
+                assert np.array_equal(out_b, O.gemm_s8_kn(Ab, Bb))
+            elif prec == "int4":
+                assert np.array_equal(out_b, O.gemm_s4(Ab, Bb, K, threads=8))
+            else:
+                ref = O.gemm_f16_f64(Ab, Bb, b_kn=(prec != "fp16_nk"), threads=8)
+                assert np.abs(out_b - ref).max() <= f16_tol(Ab, Bb, K)
