@@ -5,7 +5,7 @@
 // Blackwell-native design:
 //
 //   * persistent CTAs (grid <= #SMs), static round-robin over output tiles,
-//     grouped rasterisation (kGroupM tile-rows per band) for L2 reuse;
+//     grouped rasterisation (bands of tile-rows) for L2 reuse;
 //   * warp specialisation, 192 threads:
 //       warp 0 lane 0  -- TMA producer: 128-byte-swizzled A and B tiles into a
 //                         kStages-deep shared-memory ring (full/empty mbarriers);
@@ -30,7 +30,6 @@ namespace tcg {
 constexpr int kBM = 128;        // UMMA M (one CTA, cta_group::1)
 constexpr int kBKBytes = 128;   // bytes of K per ring stage (one swizzle row)
 constexpr int kThreads = 192;   // 6 warps
-constexpr int kGroupM = 16;     // tile-rows per rasterisation band
 
 constexpr uint32_t kErrWaitTimeout = 1;  // failure code in the high word
 
@@ -43,6 +42,9 @@ struct GemmParams {
     long long batch_stride_c;  // elements
     int M, N, K, batches;
     int tiles_m, tiles_n, num_kb;
+    int group_m;               // tile-rows per rasterisation band
+    int k_alternate;           // odd tiles of a unit walk K backwards (exact kinds only)
+    int l2_a, l2_b;            // L2 eviction priority of A / B loads (l2_policy), -1 = no hint
     int vec_store;             // C rows 16-byte aligned (N % 4 == 0, C aligned)
     unsigned long long timeout_ns;
 };
@@ -74,15 +76,19 @@ struct GemmTraits {
     static_assert(2 * kStages + 5 <= 30, "barrier area");
 };
 
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& b, int& tm, int& tn)
+// Tile t -> (batch, tile-row, tile-col): bands of `group_m` tile-rows, walked
+// column by column, so the units running at one time share a few A panels
+// and a few B panels.
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int& b, int& tm,
+                                            int& tn)
 {
     const int per_batch = tiles_m * tiles_n;
     b = t / per_batch;
     const int r = t - b * per_batch;
-    const int band = kGroupM * tiles_n;
+    const int band = group_m * tiles_n;
     const int g = r / band;
-    const int first_m = g * kGroupM;
-    const int gsz = min(tiles_m - first_m, kGroupM);
+    const int first_m = g * group_m;
+    const int gsz = min(tiles_m - first_m, group_m);
     const int rr = r - g * band;
     tm = first_m + rr % gsz;
     tn = rr / gsz;
@@ -232,12 +238,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         int stage = 0;
         uint32_t phase = 0;
         bool aborted = false;
-        for (int t = unit; t < num_tiles && !aborted; t += units) {
+        int local = 0;
+        const bool hint = p.l2_a >= 0 || p.l2_b >= 0;
+        const uint64_t pol_a = l2_policy(p.l2_a);
+        const uint64_t pol_b = l2_policy(p.l2_b);
+        for (int t = unit; t < num_tiles && !aborted; t += units, ++local) {
             int b, tm, tn;
-            tile_coords(t, p.tiles_m, p.tiles_n, b, tm, tn);
+            tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, b, tm, tn);
             const int a_row = tm * T::kTileM + static_cast<int>(rank) * kBM;
             const int b_row = tn * kBN + static_cast<int>(rank) * T::kBRows;
+            // Units advance through their tiles in step, so the whole grid
+            // finishes a wave of tiles at about the same K.  Walking K
+            // backwards on every other wave starts each wave on the K range
+            // the previous wave just brought into L2.  Integer accumulation is
+            // exact in any order; floating-point kinds keep one order.
+            const bool reverse = p.k_alternate && (local & 1);
             for (int kb = 0; kb < p.num_kb; ++kb) {
+                const int kc = reverse ? p.num_kb - 1 - kb : kb;
                 const uint32_t fb_local = smem_u32(&full[stage]);
                 if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.timeout_ns,
                                   (blockIdx.x << 8) | 0x10u | stage)) {
@@ -249,25 +266,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if constexpr (kPair) {
                     const uint32_t fb = mapa_shared(fb_local, 0);  // the leader's full barrier
                     if (leader) mbar_arrive_expect_tx(fb_local, T::kTxBytes);
-                    tma_load_3d_pair(a_dst, &tmA, fb, kb * T::kBK, a_row, b);
+                    if (hint)
+                        tma_load_3d_pair_hint(a_dst, &tmA, fb, kc * T::kBK, a_row, b, pol_a);
+                    else
+                        tma_load_3d_pair(a_dst, &tmA, fb, kc * T::kBK, a_row, b);
                     if constexpr (kBMn) {
 #pragma unroll
-                        for (int j = 0; j < T::kBRows / T::kAtomN; ++j)
-                            tma_load_3d_pair(b_dst + j * T::kBoxBytesMn, &tmB, fb, b_row + j * T::kAtomN,
-                                             kb * T::kBK, b);
+                        for (int j = 0; j < T::kBRows / T::kAtomN; ++j) {
+                            if (hint)
+                                tma_load_3d_pair_hint(b_dst + j * T::kBoxBytesMn, &tmB, fb,
+                                                      b_row + j * T::kAtomN, kc * T::kBK, b, pol_b);
+                            else
+                                tma_load_3d_pair(b_dst + j * T::kBoxBytesMn, &tmB, fb, b_row + j * T::kAtomN,
+                                                 kc * T::kBK, b);
+                        }
                     } else {
-                        tma_load_3d_pair(b_dst, &tmB, fb, kb * T::kBK, b_row, b);
+                        if (hint)
+                            tma_load_3d_pair_hint(b_dst, &tmB, fb, kc * T::kBK, b_row, b, pol_b);
+                        else
+                            tma_load_3d_pair(b_dst, &tmB, fb, kc * T::kBK, b_row, b);
                     }
                 } else {
                     mbar_arrive_expect_tx(fb_local, T::kTxBytes);
-                    tma_load_3d(a_dst, &tmA, fb_local, kb * T::kBK, a_row, b);
+                    if (hint)
+                        tma_load_3d_hint(a_dst, &tmA, fb_local, kc * T::kBK, a_row, b, pol_a);
+                    else
+                        tma_load_3d(a_dst, &tmA, fb_local, kc * T::kBK, a_row, b);
                     if constexpr (kBMn) {
 #pragma unroll
-                        for (int j = 0; j < T::kBRows / T::kAtomN; ++j)
-                            tma_load_3d(b_dst + j * T::kBoxBytesMn, &tmB, fb_local, b_row + j * T::kAtomN,
-                                        kb * T::kBK, b);
+                        for (int j = 0; j < T::kBRows / T::kAtomN; ++j) {
+                            if (hint)
+                                tma_load_3d_hint(b_dst + j * T::kBoxBytesMn, &tmB, fb_local,
+                                                 b_row + j * T::kAtomN, kc * T::kBK, b, pol_b);
+                            else
+                                tma_load_3d(b_dst + j * T::kBoxBytesMn, &tmB, fb_local, b_row + j * T::kAtomN,
+                                            kc * T::kBK, b);
+                        }
                     } else {
-                        tma_load_3d(b_dst, &tmB, fb_local, kb * T::kBK, b_row, b);
+                        if (hint)
+                            tma_load_3d_hint(b_dst, &tmB, fb_local, kc * T::kBK, b_row, b, pol_b);
+                        else
+                            tma_load_3d(b_dst, &tmB, fb_local, kc * T::kBK, b_row, b);
                     }
                 }
                 issued |= 1u << stage;
@@ -362,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             tc_fence_after();
             int b, tm, tn;
-            tile_coords(t, p.tiles_m, p.tiles_n, b, tm, tn);
+            tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, b, tm, tn);
             const int row = tm * T::kTileM + static_cast<int>(rank) * kBM + quarter * 32 + lane;
             const int col0 = tn * kBN;
             uint32_t* crow = Cbits + static_cast<long long>(b) * p.batch_stride_c +

@@ -10,6 +10,8 @@
 
 #include <atomic>
 #include <cstdio>
+#include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -100,42 +102,84 @@ tcg_status encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
     return TCG_SUCCESS;
 }
 
-// Tile shape.  Candidates: single-CTA 128 x BN tiles (BN in 64/128/256, one
-// per SM) and CTA-pair 256 x BN tiles (BN in 128/256, one pair per two SMs).
-// Cost = waves of persistent units x BN: the critical path in units of one
-// SM's 128-column share of a tile.  Pairs read a third less operand data per
-// MAC from L2 than single 128 x 256 tiles, so they win ties; a narrower or
-// single-CTA shape must save more than 3 % to be chosen.
+// Tile shape.  Candidates: CTA-pair 256 x BN tiles (BN 256/128, one pair per
+// two SMs) and single-CTA 128 x BN tiles (BN 256/128/64, one per SM).
+// Cost = waves of persistent units x BN / efficiency, the critical path in
+// units of one SM's 128-column share of a tile, where efficiency is the
+// measured per-SM throughput of the shape relative to the 256 x 256 pair
+// (int8 on B200, 4096..16384 cubed: the pair reads a third less operand data
+// per MAC than a single 128 x 256 tile, and 128-wide tiles issue half-width
+// MMAs).  Ties go to the earlier (more efficient) shape.
 struct TileChoice {
     int bn;
     bool pair;
 };
 
-TileChoice choose_tile(int M, int N, int batches, int sms, bool i8_mn)
+// Environment overrides (read once; the tcg_set_* calls take precedence):
+// TCG_TILE_N = 64|128|256, TCG_CTA_PAIR = 1 (single) | 2 (pair),
+// TCG_GROUP_M = band height in tiles, TCG_K_ALT = 0|1.
+int env_int(const char* name, int dflt = 0)
 {
-    const int forced_bn = g_force_bn.load();
-    const int forced_pair = g_force_pair.load();  // 0 auto, 1 single, 2 pair
+    const char* v = std::getenv(name);
+    return v ? std::atoi(v) : dflt;
+}
+
+TileChoice choose_tile(int M, int N, int K, int elem_bytes, int batches, int sms, bool i8_mn)
+{
+    static const int env_bn = env_int("TCG_TILE_N");
+    static const int env_pair = env_int("TCG_CTA_PAIR");
+    const int forced_bn = g_force_bn.load() ? g_force_bn.load() : env_bn;
+    const int forced_pair = g_force_pair.load() ? g_force_pair.load() : env_pair;  // 0 auto, 1 single, 2 pair
+    struct Cand {
+        bool pair;
+        int bn;
+        double eff;
+    };
+    static const Cand cands[] = {{true, 256, 1.00}, {false, 256, 0.87}, {true, 128, 0.72},
+                                 {false, 128, 0.72}, {false, 64, 0.50}};
+    // Measured on B200: once the operand panels one wave of pair tiles streams
+    // (about 4400 rows x K bytes at 256 x 256) no longer fit in L2, pair
+    // tiles pull about twice the DRAM bytes of single-CTA tiles and lose to
+    // them (int8 32768^3: 59 GB vs 29 GB per launch, 2.2 vs 2.5 POPS
+    // sustained).  Such problems use single-CTA tiles.
+    const double wave_bytes = 4400.0 * static_cast<double>(K) * elem_bytes;
+    const long long pair_tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256) * batches;
+    const bool pair_thrashes = wave_bytes > 100e6 && pair_tiles >= 4LL * (sms / 2);
     TileChoice best{256, true};
     double best_cost = -1.0;
-    for (int pair = 1; pair >= 0; --pair) {
-        if ((forced_pair == 1 && pair) || (forced_pair == 2 && !pair)) continue;
-        for (int bn : {256, 128, 64}) {
-            if (pair && bn == 64) continue;
-            if (i8_mn && (pair ? bn / 2 : bn) < 128) continue;  // whole 128-byte atoms
-            if (forced_bn && bn != forced_bn) continue;
-            const long long tm = (M + (pair ? 255 : 127)) / (pair ? 256 : 128);
-            const long long tiles = tm * ((N + bn - 1) / bn) * batches;
-            const long long units = pair ? sms / 2 : sms;
-            const long long waves = (tiles + units - 1) / units;
-            const double cost = static_cast<double>(waves) * bn;
-            if (best_cost < 0 || cost < best_cost * 0.97) {
-                best = TileChoice{bn, pair != 0};
-                best_cost = cost;
-            }
+    for (const Cand& c : cands) {
+        if ((forced_pair == 1 && c.pair) || (forced_pair == 2 && !c.pair)) continue;
+        if (!forced_pair && c.pair && pair_thrashes) continue;
+        if (forced_bn && c.bn != forced_bn) continue;
+        if (i8_mn && (c.pair ? c.bn / 2 : c.bn) < 128) continue;  // whole 128-byte atoms
+        const long long tm = (M + (c.pair ? 255 : 127)) / (c.pair ? 256 : 128);
+        const long long tiles = tm * ((N + c.bn - 1) / c.bn) * batches;
+        const long long units = c.pair ? sms / 2 : sms;
+        const long long waves = (tiles + units - 1) / units;
+        const double cost = static_cast<double>(waves) * c.bn / c.eff;
+        if (best_cost < 0 || cost < best_cost) {
+            best = TileChoice{c.bn, c.pair};
+            best_cost = cost;
         }
     }
     if (best_cost < 0) best = TileChoice{forced_bn ? forced_bn : 256, forced_pair != 1};
     return best;
+}
+
+// Band height: about square in elements, gm * tile_m ~ gn * BN with gm * gn =
+// the units running at once, so a wave touches as few operand panels as it
+// can (pair 256 x 256: 8; single 128 x 256: 16).
+int choose_group_m(int tile_m, int bn, int units, int tiles_m)
+{
+    static const int env_g = env_int("TCG_GROUP_M");
+    int g = env_g;
+    if (g <= 0) {
+        const double ideal = std::sqrt(static_cast<double>(units) * bn / tile_m);
+        g = 1;
+        while (g * 2 <= ideal) g *= 2;
+    }
+    if (g > tiles_m) g = tiles_m;
+    return g < 1 ? 1 : g;
 }
 
 template <bool kI8, bool kAccF16, bool kBMn, int kBN, bool kPair>
@@ -170,6 +214,15 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     p.tiles_m = (M + T::kTileM - 1) / T::kTileM;
     p.tiles_n = (N + kBN - 1) / kBN;
     p.num_kb = (K + T::kBK - 1) / T::kBK;
+    p.group_m = choose_group_m(T::kTileM, kBN, kPair ? dev.sms / 2 : dev.sms, p.tiles_m);
+    static const int env_kalt = env_int("TCG_K_ALT", 1);
+    p.k_alternate = (kI8 && env_kalt) ? 1 : 0;
+    // Optional L2 eviction priorities for the A / B loads (-1 = no hint, the
+    // default: on B200 the hinted loads doubled DRAM traffic at 32768^3).
+    static const int env_l2a = env_int("TCG_L2_A", -1);
+    static const int env_l2b = env_int("TCG_L2_B", -1);
+    p.l2_a = env_l2a;
+    p.l2_b = env_l2b;
     p.vec_store = ((N % 4) == 0 && (reinterpret_cast<uintptr_t>(C) % 16) == 0) ? 1 : 0;
     p.timeout_ns = g_timeout_ns.load();
 
@@ -204,6 +257,10 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
         }
         const long long units = max_clusters[dev_id] < pairs ? max_clusters[dev_id] : pairs;
         cfg.gridDim = dim3(static_cast<unsigned>(2 * (tiles < units ? tiles : units)), 1, 1);
+        static const int debug = env_int("TCG_DEBUG");
+        if (debug)
+            std::fprintf(stderr, "tcgemm: pair grid %u (max clusters %d) tile 256x%d stages %d group_m %d kalt %d\n",
+                         cfg.gridDim.x, max_clusters[dev_id], kBN, kStages, p.group_m, p.k_alternate);
         e = cudaLaunchKernelEx(&cfg, kern, mA, mB, p);
         if (e != cudaSuccess) return cuda_fail(e);
     } else {
@@ -221,7 +278,7 @@ template <bool kI8, bool kAccF16, bool kBMn>
 tcg_status dispatch_bn(DeviceState& dev, const void* A, const void* B, void* C, int M, int N, int K,
                        int batches, cudaStream_t st)
 {
-    const TileChoice c = choose_tile(M, N, batches, dev.sms, kI8 && kBMn);
+    const TileChoice c = choose_tile(M, N, K, kI8 ? 1 : 2, batches, dev.sms, kI8 && kBMn);
     if (c.pair) {
         if (c.bn == 128) {
             // an MN-major int8 pair tile needs 128 columns per CTA

@@ -392,7 +392,7 @@ def test_runs_on_current_stream():
 
 # ------------------------------------------------- tile shapes & CTA pairs --
 
-_SHAPE_CASES = [(1, 300, 520, 384), (2, 260, 136, 128), (1, 512, 1024, 256)]
+_SHAPE_CASES = [(1, 300, 528, 384), (2, 260, 144, 128), (1, 512, 1024, 256)]
 
 
 @pytest.mark.parametrize("prec", ["int8", "int8_kn", "int4", "fp16", "fp16_nk", "fp16acc"])
