@@ -12,9 +12,9 @@ GPU this is the full 32768^3 problem on one B200.
 
 A "step" is one GEMM of each rank's slice.  ``value`` is whole-job TOPS with
 inputs resident in HBM (inputs are 2 GiB, larger than L2, so no flush is
-needed); ``e2e`` is the same metric through the public Python API with the
-step's A slice and B copied from pinned host memory and its C slice copied
-back inside the timed region.  Device time is measured with CUDA events on
+needed); ``e2e`` is the same metric through the public host-buffer API
+(``gemm_int8_host``) with the step's A slice and B copied from pinned host
+memory and its C slice copied back inside the timed region.  Device time is measured with CUDA events on
 the launching stream, max over ranks.
 
 ``--impl reference`` times the reference's own CPU GEMM (src/data_int8.cu
@@ -229,9 +229,14 @@ def run_ours(args):
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
+    from tensorcoreptx_b200.dist import max_over_ranks as _max_over_ranks
+    from tensorcoreptx_b200.dist import shard_rows
+
     size = args.size
-    assert size % world == 0, "size must divide evenly across ranks"
-    rows = size // world
+    r0, r1 = shard_rows(size, world, rank, align=256)
+    rows = r1 - r0
+    if args.gather and size % world != 0:
+        raise SystemExit("--gather needs the rows to divide evenly across ranks")
     ops_total = 2.0 * size * size * size
     ops_rank = 2.0 * rows * size * size
 
@@ -240,11 +245,7 @@ def run_ours(args):
             dist.barrier()
 
     def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return _max_over_ranks(x, device=dev)
 
     # inputs: A slice of this rank, full B (BT layout, N x K), seeded on the GPU
     g = torch.Generator(device=dev).manual_seed(1234)
@@ -315,10 +316,9 @@ def run_ours(args):
     torch.cuda.empty_cache()
 
     def e2e_step():
-        Ad = A_h.to(dev, non_blocking=True)
-        Bd = B_h.to(dev, non_blocking=True)
-        Cd = T.gemm_int8(Ad, Bd)
-        C_h.copy_(Cd, non_blocking=True)
+        # public host-buffer entry: pinned A slice and B in, pinned C slice out,
+        # row chunks of C pipelined against the copies
+        T.gemm_int8_host(A_h, B_h, out=C_h, chunks=8)
 
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):

@@ -81,3 +81,16 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_native, "LIB_PATH", str(tmp_path / "absent.so"))
     with pytest.raises(ImportError, match="missing"):
         _native.lib()
+
+
+def test_host_entry_validation():
+    import torch
+    import tensorcoreptx_b200 as T
+    with pytest.raises(RuntimeError, match="must be int8"):
+        T.gemm_int8_host(torch.zeros(4, 16), torch.zeros(4, 16, dtype=torch.int8))
+    with pytest.raises(RuntimeError, match="A cols must equal BT cols"):
+        T.gemm_int8_host(torch.zeros(4, 16, dtype=torch.int8), torch.zeros(4, 32, dtype=torch.int8))
+    from tensorcoreptx_b200.host_gemm import _row_chunks
+    assert _row_chunks(1000, 3) == [(0, 512), (512, 1000)]
+    assert _row_chunks(100, 8) == [(0, 100)]
+    assert _row_chunks(4096, 8) == [(r, r + 512) for r in range(0, 4096, 512)]

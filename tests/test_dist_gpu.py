@@ -1,0 +1,60 @@
+"""Row-sharded GEMM over NCCL on 2 GPUs (skipped with fewer GPUs): every
+rank's gathered C equals the single-GPU product of the full matrices."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    from tensorcoreptx_b200.dist import shard_rows, sharded_gemm_int8
+    import tensorcoreptx_b200 as T
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=120))
+        M, N, K = 1024, 768, 512
+        g = torch.Generator(device=dev).manual_seed(7)  # identical inputs on every rank
+        A = torch.randint(-128, 128, (M, K), generator=g, device=dev, dtype=torch.int8)
+        BT = torch.randint(-128, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
+        r0, r1 = shard_rows(M, world, rank, align=256)
+        C = sharded_gemm_int8(A[r0:r1].contiguous(), BT, gather=True)
+        ok = bool(torch.equal(C, T.gemm_int8(A, BT)))
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, ok, ""))
+    except Exception as e:  # pragma: no cover
+        q.put((rank, False, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sharded_gather_two_gpus():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok, err in res:
+        assert ok, (rank, err)

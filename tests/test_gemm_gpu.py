@@ -451,3 +451,22 @@ def test_every_tile_shape_gives_identical_results(prec):
             else:
                 ref = O.gemm_f16_f64(Ab, Bb, b_kn=(prec != "fp16_nk"), threads=8)
                 assert np.abs(out_b - ref).max() <= f16_tol(Ab, Bb, K)
+
+
+# ------------------------------------------------------- host-buffer entry --
+
+@pytest.mark.parametrize("M,N,K,chunks", [(1000, 384, 256, 3), (200, 128, 64, 8), (2048, 512, 512, 8)])
+def test_host_pipeline_matches_device_path(M, N, K, chunks):
+    T = tcg()
+    rng = np.random.default_rng(M + N)
+    A = torch.from_numpy(rand_s8(rng, (M, K))).pin_memory()
+    BT = torch.from_numpy(rand_s8(rng, (N, K))).pin_memory()
+    C = T.gemm_int8_host(A, BT, chunks=chunks)
+    torch.cuda.current_stream().synchronize()
+    assert np.array_equal(C.numpy(), O.gemm_s8(A.numpy(), BT.numpy(), threads=8))
+    Ah = torch.from_numpy(rand_f16_bits(rng, (M, K))).view(torch.float16).pin_memory()
+    Bh = torch.from_numpy(rand_f16_bits(rng, (K, N))).view(torch.float16).pin_memory()
+    Cf = T.gemm_fp16_host(Ah, Bh, chunks=chunks)
+    torch.cuda.current_stream().synchronize()
+    ref = T.gemm_fp16(Ah.cuda(), Bh.cuda()).cpu()
+    assert torch.equal(Cf, ref)
