@@ -46,7 +46,9 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--size", type=int, default=SIZE, help="M = N = K of the whole problem")
-    ap.add_argument("--gather", action="store_true", help="all-gather C over NCCL each step")
+    ap.add_argument("--gather", choices=["none", "nccl", "p2p"], default="none",
+                    help="all-gather C each step: NCCL after the GEMM, or peer stores from the "
+                         "GEMM epilogue (p2p)")
     ap.add_argument("--no-extras", action="store_true", help="skip the per-config extras")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0,
@@ -235,7 +237,8 @@ def run_ours(args):
     size = args.size
     r0, r1 = shard_rows(size, world, rank, align=256)
     rows = r1 - r0
-    if args.gather and size % world != 0:
+    gather = args.gather if world > 1 else "none"
+    if gather != "none" and size % world != 0:
         raise SystemExit("--gather needs the rows to divide evenly across ranks")
     ops_total = 2.0 * size * size * size
     ops_rank = 2.0 * rows * size * size
@@ -255,16 +258,27 @@ def run_ours(args):
     g.manual_seed(999)  # identical B on every rank (replicated)
     BT = torch.randint(-128, 128, (size, size), generator=g, device=dev, dtype=torch.int8)
     C = torch.empty(rows, size, dtype=torch.int32, device=dev)
-    C_full = torch.empty(size, size, dtype=torch.int32, device=dev) if (args.gather and world > 1) else None
+    C_full = torch.empty(size, size, dtype=torch.int32, device=dev) if gather == "nccl" else None
+    peer = None
+    if gather == "p2p":
+        from tensorcoreptx_b200.dist import PeerGather
+        peer = PeerGather(size, size, dev)
 
     from tensorcoreptx_b200 import _native as nat
     lib = nat.lib()
     stream = torch.cuda.Stream(device=dev)
 
-    def step():
+    def gemm_launch():
+        if peer is not None:
+            with torch.cuda.stream(stream):
+                peer.gemm_int8(A, BT, r0)  # GEMM + epilogue stores to every rank + 1-word barrier
+            return
         st = lib.tcg_gemm_s8(A.data_ptr(), BT.data_ptr(), C.data_ptr(), rows, size, size, 1,
                              nat.TCG_B_NK, stream.cuda_stream)
         nat.check("tcg_gemm_s8", st)
+
+    def step():
+        gemm_launch()
         if C_full is not None:
             with torch.cuda.stream(stream):
                 dist.all_gather_into_tensor(C_full, C)
@@ -290,9 +304,7 @@ def run_ours(args):
     t_begin.record(stream)
     for i in range(args.steps):
         ev[i][0].record(stream)
-        st = lib.tcg_gemm_s8(A.data_ptr(), BT.data_ptr(), C.data_ptr(), rows, size, size, 1,
-                             nat.TCG_B_NK, stream.cuda_stream)
-        nat.check("tcg_gemm_s8", st)
+        gemm_launch()
         ev[i][1].record(stream)
         if C_full is not None:
             with torch.cuda.stream(stream):
@@ -308,6 +320,9 @@ def run_ours(args):
     werr = T.check_device_error(stream)
     assert werr == 0
 
+    if peer is not None:
+        peer.close()
+        del peer
     # ---- end-to-end through the public API: pinned host in, pinned host out
     A_h = A.cpu().pin_memory()
     B_h = BT.cpu().pin_memory()
@@ -372,7 +387,9 @@ def run_ours(args):
             "data": "synthetic",
             "config": {
                 "workload": f"int8 GEMM M=N=K={size}, A row-sharded over {world} GPU(s), "
-                            f"B replicated, int32 C" + (", C all-gathered" if C_full is not None else ""),
+                            f"B replicated, int32 C" + {"none": "", "nccl": ", C all-gathered (NCCL)",
+                                                         "p2p": ", C all-gathered by the GEMM epilogue "
+                                                                "over NVLink peer stores"}[gather],
                 "per_rank": f"{rows}x{size}x{size}",
                 "values": "int8 uniform [-128,127], seeded",
                 "l2": "inputs (2 GiB) larger than L2; no flush",
@@ -391,7 +408,7 @@ def run_ours(args):
             },
             "e2e": {"value": ops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * (1 if C_full is None else 2),
+            "gpu_launches": args.steps,
             "clocks": clocks.summary(),
         }
 
@@ -487,6 +504,11 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)
+    # Libraries (NCCL's version banner, for one) may print to stdout; keep
+    # stdout for the one JSON line by sending everything else to stderr.
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
     result = run_ours(args)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -495,7 +517,8 @@ def main():
             result["cpu_baseline"] = cpu_baseline_line(args)
         if world == 1 and not args.no_extras:
             result["extras"] = extras()
-        print(json.dumps(result), flush=True)
+        sys.stdout.flush()
+        os.write(json_fd, (json.dumps(result) + "\n").encode())
     return 0
 
 

@@ -64,6 +64,25 @@ tcg_status tcg_gemm_s8(const int8_t* A, const int8_t* B, int32_t* C,
                        int M, int N, int K, int batches,
                        tcg_b_layout b_layout, void* stream);
 
+/* int8 GEMM whose epilogue writes the M x N result to every one of C_dst[0..
+ * n_dst-1] (1 <= n_dst <= 8): C_dst[0] is local; the others may be peer GPUs'
+ * buffers mapped with tcg_ipc_open, reached with NVLink stores from the same
+ * epilogue, so an all-gather of row-sharded C overlaps the tensor-core work
+ * tile by tile.  The caller orders readers of peer buffers after this launch
+ * (e.g. a collective barrier on the same stream).  No counterpart in the
+ * reference, which has no multi-GPU path. */
+tcg_status tcg_gemm_s8_multi(const int8_t* A, const int8_t* B, int32_t* const* C_dst, int n_dst,
+                             int M, int N, int K, tcg_b_layout b_layout, void* stream);
+
+/* Cross-process peer mapping (CUDA IPC) for tcg_gemm_s8_multi destinations.
+ * tcg_ipc_handle: 64-byte handle of the allocation holding `ptr`, and ptr's
+ * offset in it.  tcg_ipc_open: map another process's allocation into the
+ * current device's address space (base of the allocation; add the offset).
+ * tcg_ipc_close: unmap a base returned by tcg_ipc_open. */
+tcg_status tcg_ipc_handle(const void* ptr, void* handle, size_t* offset);
+tcg_status tcg_ipc_open(const void* handle, void** base);
+tcg_status tcg_ipc_close(void* base);
+
 /* packed int4 x int4 -> int32, exact; B is always BT (N x K/2 bytes).
  * Replaces int4 launch_kernel: kernels/int4_wmma.cu:148-158,
  * kernels/int4_ptx_mma_k64_x4_x2nontrans_ca.cu:168-178.

@@ -27,6 +27,10 @@ _p, _i, _sz = C.c_void_p, C.c_int, C.c_size_t
 SIGNATURES = {
     "tcg_gemm_f16": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _i, _i, _p]),
     "tcg_gemm_s8": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _i, _p]),
+    "tcg_gemm_s8_multi": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _i, _p]),
+    "tcg_ipc_handle": (C.c_int, [_p, _p, C.POINTER(C.c_size_t)]),
+    "tcg_ipc_open": (C.c_int, [_p, C.POINTER(C.c_void_p)]),
+    "tcg_ipc_close": (C.c_int, [_p]),
     "tcg_gemm_s4_workspace_size": (_sz, [_i, _i, _i, _i]),
     "tcg_gemm_s4": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _p, _sz, _p]),
     "tcg_unpack_s4": (C.c_int, [_p, _p, _sz, _p]),

@@ -32,6 +32,7 @@ constexpr int kBKBytes = 128;   // bytes of K per ring stage (one swizzle row)
 constexpr int kThreads = 192;   // 6 warps
 
 constexpr uint32_t kErrWaitTimeout = 1;  // failure code in the high word
+constexpr int kMaxExtraDst = 7;          // peer destinations of one GEMM's C
 
 // Failure word, one per device.  This header is compiled into exactly one
 // translation unit (tcgemm.cu), which owns the definition.
@@ -45,6 +46,8 @@ struct GemmParams {
     int group_m;               // tile-rows per rasterisation band
     int k_alternate;           // odd tiles of a unit walk K backwards (exact kinds only)
     int l2_a, l2_b;            // L2 eviction priority of A / B loads (l2_policy), -1 = no hint
+    int n_extra;               // further destinations of C (peer GPUs' buffers), <= kMaxExtraDst
+    void* extra[7];            // each receives the same tile at the same offset as C
     int vec_store;             // C rows 16-byte aligned (N % 4 == 0, C aligned)
     unsigned long long timeout_ns;
 };
@@ -69,7 +72,8 @@ struct GemmTraits {
         make_idesc(kI8 ? 2u : (kAccF16 ? 0u : 1u), kI8 ? 1u : 0u, kBMn, kTileM, kBN);
     static constexpr int kEpiArrivals = kPair ? 8 : 4;  // one per epilogue warp (of both CTAs)
     static constexpr int kBarrierBytes = 256;
-    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
+    static constexpr int kEpiStageBytes = 4 * 32 * 32 * 4;  // a 32 x 32 word tile per epilogue warp
+    static constexpr int kSmemBytes = kStages * kStageBytes + kEpiStageBytes + 1024 + kBarrierBytes;
     static_assert(kBRows % kAtomN == 0 || !kBMn, "MN-major B needs whole 128-byte atoms");
     static_assert(kTmemCols >= 32 && kTmemCols <= 512, "TMEM allocation");
     static_assert(kSmemBytes <= 232448, "shared memory per CTA");
@@ -181,7 +185,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * T::kStageBytes);
+    uint32_t* epi_stage = reinterpret_cast<uint32_t*>(smem + kStages * T::kStageBytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * T::kStageBytes + T::kEpiStageBytes);
     uint64_t* full = bars;
     uint64_t* empty = bars + kStages;
     uint64_t* tfull = bars + 2 * kStages;
@@ -389,9 +394,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 2) {
         // ---------------------------------------------------- epilogue ----
+        // Each warp owns 32 rows of the tile (its TMEM lane quarter).  Per 32
+        // columns: tcgen05.ld gives lane i row i; the words go through a
+        // 32 x 32 shared-memory tile (16-byte chunks XOR-swizzled by row, so
+        // neither pass has bank conflicts) and come back as 4 rows x 32
+        // columns per instruction, i.e. every global store instruction writes
+        // four whole 128-byte row segments -- of the local C and, for the
+        // epilogue all-gather, of every peer's C over NVLink.
         const int quarter = warp & 3;  // TMEM lanes this warp may read
         uint32_t* Cbits = static_cast<uint32_t*>(p.C);
+        uint32_t* stile = epi_stage + (warp - 2) * 32 * 32;
         const uint32_t tempty_leader0 = kPair ? mapa_shared(smem_u32(&tempty[0]), 0) : smem_u32(&tempty[0]);
+        const int rsub = lane >> 3;  // row within a 4-row group on the way out
+        const int csub = lane & 7;   // 16-byte chunk (4 columns) within the 32 columns
         int local = 0;
         for (int t = unit; t < num_tiles; t += units, ++local) {
             const int acc = local & 1;
@@ -402,10 +417,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             int b, tm, tn;
             tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, b, tm, tn);
-            const int row = tm * T::kTileM + static_cast<int>(rank) * kBM + quarter * 32 + lane;
+            const int row0 = tm * T::kTileM + static_cast<int>(rank) * kBM + quarter * 32;
             const int col0 = tn * kBN;
-            uint32_t* crow = Cbits + static_cast<long long>(b) * p.batch_stride_c +
-                             static_cast<long long>(row) * p.N;
+            const long long cbase = static_cast<long long>(b) * p.batch_stride_c;
             const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                     static_cast<uint32_t>(acc * kBN);
 #pragma unroll 1
@@ -420,18 +434,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 32; ++j)
                         v[j] = __float_as_uint(__half2float(__ushort_as_half(static_cast<unsigned short>(v[j] & 0xFFFFu))));
                 }
-                if (row < p.M) {
-                    if (p.vec_store && col + 32 <= p.N) {
-                        uint4* dst = reinterpret_cast<uint4*>(crow + col);
 #pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            dst[j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (col + j < p.N) crow[col + j] = v[j];
+                for (int q = 0; q < 8; ++q)
+                    *reinterpret_cast<uint4*>(stile + lane * 32 + ((q ^ (lane & 7)) << 2)) =
+                        make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                __syncwarp();
+                const int gcol = col + csub * 4;
+#pragma unroll 2
+                for (int it = 0; it < 8; ++it) {
+                    const int r = it * 4 + rsub;
+                    const uint4 w = *reinterpret_cast<const uint4*>(stile + r * 32 + ((csub ^ (r & 7)) << 2));
+                    const int grow = row0 + r;
+                    if (grow < p.M && gcol < p.N) {
+                        const long long off = cbase + static_cast<long long>(grow) * p.N + gcol;
+#pragma unroll 1
+                        for (int d = -1; d < p.n_extra; ++d) {
+                            uint32_t* dst = (d < 0 ? Cbits : static_cast<uint32_t*>(p.extra[d])) + off;
+                            if (p.vec_store && gcol + 4 <= p.N) {
+                                *reinterpret_cast<uint4*>(dst) = w;
+                            } else {
+                                dst[0] = w.x;
+                                if (gcol + 1 < p.N) dst[1] = w.y;
+                                if (gcol + 2 < p.N) dst[2] = w.z;
+                                if (gcol + 3 < p.N) dst[3] = w.w;
+                            }
+                        }
                     }
                 }
+                __syncwarp();  // the tile is rewritten by the next 32 columns
             }
             tc_fence_before();
             __syncwarp();
@@ -445,6 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
+    if (p.n_extra > 0) __threadfence_system();  // peer stores performed before the kernel ends
     __syncwarp();
     tc_fence_before();
     __syncthreads();

@@ -184,7 +184,7 @@ int choose_group_m(int tile_m, int bn, int units, int tiles_m)
 
 template <bool kI8, bool kAccF16, bool kBMn, int kBN, bool kPair>
 tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, int M, int N, int K,
-                       int batches, cudaStream_t st)
+                       int batches, cudaStream_t st, void* const* extra = nullptr, int n_extra = 0)
 {
     constexpr int kStages = kPair ? (kBN == 256 ? 6 : 8) : (kBN == 256 ? 4 : (kBN == 128 ? 6 : 8));
     using T = GemmTraits<kI8, kAccF16, kBMn, kBN, kStages, kPair>;
@@ -223,6 +223,12 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     static const int env_l2b = env_int("TCG_L2_B", -1);
     p.l2_a = env_l2a;
     p.l2_b = env_l2b;
+    p.n_extra = n_extra;
+    for (int i = 0; i < kMaxExtraDst; ++i) p.extra[i] = i < n_extra ? extra[i] : nullptr;
+    if (n_extra > 0) {  // every destination must take 16-byte stores like C
+        for (int i = 0; i < n_extra; ++i)
+            if ((reinterpret_cast<uintptr_t>(extra[i]) & 15u) != 0) p.vec_store = 0;
+    }
     p.vec_store = ((N % 4) == 0 && (reinterpret_cast<uintptr_t>(C) % 16) == 0) ? 1 : 0;
     p.timeout_ns = g_timeout_ns.load();
 
@@ -276,22 +282,22 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
 
 template <bool kI8, bool kAccF16, bool kBMn>
 tcg_status dispatch_bn(DeviceState& dev, const void* A, const void* B, void* C, int M, int N, int K,
-                       int batches, cudaStream_t st)
+                       int batches, cudaStream_t st, void* const* extra = nullptr, int n_extra = 0)
 {
     const TileChoice c = choose_tile(M, N, K, kI8 ? 1 : 2, batches, dev.sms, kI8 && kBMn);
     if (c.pair) {
         if (c.bn == 128) {
             // an MN-major int8 pair tile needs 128 columns per CTA
-            if constexpr (!(kI8 && kBMn)) return launch_gemm<kI8, kAccF16, kBMn, 128, true>(dev, A, B, C, M, N, K, batches, st);
+            if constexpr (!(kI8 && kBMn)) return launch_gemm<kI8, kAccF16, kBMn, 128, true>(dev, A, B, C, M, N, K, batches, st, extra, n_extra);
         }
-        return launch_gemm<kI8, kAccF16, kBMn, 256, true>(dev, A, B, C, M, N, K, batches, st);
+        return launch_gemm<kI8, kAccF16, kBMn, 256, true>(dev, A, B, C, M, N, K, batches, st, extra, n_extra);
     }
     switch (c.bn) {
     case 64:
-        if constexpr (!(kI8 && kBMn)) return launch_gemm<kI8, kAccF16, kBMn, 64, false>(dev, A, B, C, M, N, K, batches, st);
+        if constexpr (!(kI8 && kBMn)) return launch_gemm<kI8, kAccF16, kBMn, 64, false>(dev, A, B, C, M, N, K, batches, st, extra, n_extra);
         [[fallthrough]];
-    case 128: return launch_gemm<kI8, kAccF16, kBMn, 128, false>(dev, A, B, C, M, N, K, batches, st);
-    default: return launch_gemm<kI8, kAccF16, kBMn, 256, false>(dev, A, B, C, M, N, K, batches, st);
+    case 128: return launch_gemm<kI8, kAccF16, kBMn, 128, false>(dev, A, B, C, M, N, K, batches, st, extra, n_extra);
+    default: return launch_gemm<kI8, kAccF16, kBMn, 256, false>(dev, A, B, C, M, N, K, batches, st, extra, n_extra);
     }
 }
 
@@ -379,6 +385,37 @@ tcg_status tcg_gemm_s8(const int8_t* A, const int8_t* B, int32_t* C, int M, int 
     if ((s = resolve_encode()) != TCG_SUCCESS) return s;
     return b_layout == TCG_B_KN ? dispatch_bn<true, false, true>(*dev, A, B, C, M, N, K, batches, st)
                                 : dispatch_bn<true, false, false>(*dev, A, B, C, M, N, K, batches, st);
+}
+
+tcg_status tcg_gemm_s8_multi(const int8_t* A, const int8_t* B, int32_t* const* C_dst, int n_dst, int M, int N,
+                             int K, tcg_b_layout b_layout, void* stream)
+{
+    if (b_layout != TCG_B_KN && b_layout != TCG_B_NK) return TCG_ERR_ARG;
+    if (!C_dst || n_dst < 1 || n_dst > 1 + kMaxExtraDst) return TCG_ERR_ARG;
+    for (int i = 0; i < n_dst; ++i)
+        if (!C_dst[i]) return TCG_ERR_ARG;
+        else if (!aligned4(C_dst[i])) return TCG_ERR_ALIGN;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    bool done;
+    tcg_status s = prologue(A, B, C_dst[0], M, N, K, 1, st, &done);
+    if (s != TCG_SUCCESS) return s;
+    if (done) {
+        if (M > 0 && N > 0 && K == 0)  // zero-fill every destination, as for C
+            for (int i = 1; i < n_dst; ++i) {
+                cudaError_t e = cudaMemsetAsync(C_dst[i], 0, static_cast<size_t>(M) * N * 4, st);
+                if (e != cudaSuccess) return cuda_fail(e);
+            }
+        return TCG_SUCCESS;
+    }
+    if (K % 16 != 0) return TCG_ERR_SHAPE;
+    if (b_layout == TCG_B_KN && N % 16 != 0) return TCG_ERR_SHAPE;
+    DeviceState* dev;
+    if ((s = device_state(&dev)) != TCG_SUCCESS) return s;
+    if ((s = resolve_encode()) != TCG_SUCCESS) return s;
+    void* const* extra = reinterpret_cast<void* const*>(C_dst + 1);
+    return b_layout == TCG_B_KN
+               ? dispatch_bn<true, false, true>(*dev, A, B, C_dst[0], M, N, K, 1, st, extra, n_dst - 1)
+               : dispatch_bn<true, false, false>(*dev, A, B, C_dst[0], M, N, K, 1, st, extra, n_dst - 1);
 }
 
 size_t tcg_gemm_s4_workspace_size(int M, int N, int K, int batches)
@@ -513,6 +550,50 @@ tcg_status tcg_check_device_error(void* stream, uint64_t* word)
     e = cudaMemcpyToSymbol(tcg::g_tcg_error_word, &zero, sizeof zero);
     if (e != cudaSuccess) return cuda_fail(e);
     return TCG_ERR_TIMEOUT;
+}
+
+tcg_status tcg_ipc_handle(const void* ptr, void* handle, size_t* offset)
+{
+    if (!ptr || !handle || !offset) return TCG_ERR_ARG;
+    typedef CUresult (*RangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+    static RangeFn range = nullptr;
+    static std::once_flag once;
+    std::call_once(once, []() {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            range = reinterpret_cast<RangeFn>(fn);
+    });
+    if (!range) return TCG_ERR_CUDA;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    CUresult r = range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+    if (r != CUDA_SUCCESS) {
+        t_last_cuda_error = static_cast<int>(r);
+        return TCG_ERR_CUDA;
+    }
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+    if (e != cudaSuccess) return cuda_fail(e);
+    std::memcpy(handle, &h, sizeof h);
+    *offset = reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base);
+    return TCG_SUCCESS;
+}
+
+tcg_status tcg_ipc_open(const void* handle, void** base)
+{
+    if (!handle || !base) return TCG_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof h);
+    cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? TCG_SUCCESS : cuda_fail(e);
+}
+
+tcg_status tcg_ipc_close(void* base)
+{
+    cudaError_t e = cudaIpcCloseMemHandle(base);
+    return e == cudaSuccess ? TCG_SUCCESS : cuda_fail(e);
 }
 
 void tcg_set_wait_timeout_ns(uint64_t ns) { g_timeout_ns.store(ns ? ns : 2000000000ull); }

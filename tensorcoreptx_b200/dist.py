@@ -64,3 +64,82 @@ def sharded_gemm_int8(A_local: torch.Tensor, BT: torch.Tensor, gather: bool = Fa
         raise RuntimeError("gather needs equal shards: out must have world x local rows")
     dist.all_gather_into_tensor(out, C_local.contiguous(), group=group)
     return out
+
+
+class PeerGather:
+    """All-gather of row-sharded C through the GEMM epilogue.
+
+    Every rank allocates the full M x N int32 C; the buffers are mapped into
+    every other rank with CUDA IPC (tcg_ipc_*), and ``gemm_int8`` launches one
+    tcgen05 GEMM whose epilogue stores each finished tile of this rank's rows
+    into all G buffers over NVLink -- the transfer overlaps the math tile by
+    tile instead of following it as a separate NCCL all-gather.  A one-word
+    all-reduce on the same stream then orders every rank's later reads after
+    all ranks' stores.  ``close()`` (or the context manager) unmaps the peer
+    buffers; call it on every rank before destroying the process group.
+    """
+
+    def __init__(self, M: int, N: int, device: torch.device, group=None):
+        import ctypes as C
+        from . import _native as nat
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise RuntimeError("PeerGather supports up to 8 ranks")
+        self.M, self.N, self.device = M, N, device
+        self.C = torch.empty((M, N), dtype=torch.int32, device=device)
+        L = nat.lib()
+        handle = (C.c_ubyte * 64)()
+        off = C.c_size_t(0)
+        nat.check("tcg_ipc_handle", L.tcg_ipc_handle(self.C.data_ptr(), handle, C.byref(off)))
+        mine = (bytes(handle), int(off.value))
+        allh = [None] * self.world
+        dist.all_gather_object(allh, mine, group=group)
+        self._opened = []
+        self.ptrs = []
+        for r, (h, o) in enumerate(allh):
+            if r == self.rank:
+                self.ptrs.append(self.C.data_ptr())
+                continue
+            base = C.c_void_p(0)
+            buf = (C.c_ubyte * 64).from_buffer_copy(h)
+            nat.check("tcg_ipc_open", L.tcg_ipc_open(buf, C.byref(base)))
+            self._opened.append(base.value)
+            self.ptrs.append(base.value + o)
+        self._flag = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def gemm_int8(self, A_local: torch.Tensor, BT: torch.Tensor, row0: int) -> torch.Tensor:
+        """Rows [row0, row0 + A_local.shape[0]) of C = A_local x BT^T, stored
+        into every rank's full C; returns this rank's full C (complete once
+        every rank has made the same call, in stream order)."""
+        import ctypes as C
+        from . import _native as nat
+        from .gemm import _check, _stream_ptr
+        _check(A_local.is_cuda and BT.is_cuda, "A and BT must be CUDA tensors")
+        _check(A_local.dtype == torch.int8 and BT.dtype == torch.int8, "A and BT must be int8")
+        _check(A_local.is_contiguous() and BT.is_contiguous(), "A and BT must be contiguous")
+        rows, K = A_local.shape
+        _check(BT.shape == (self.N, K), "BT must be N x K")
+        _check(0 <= row0 and row0 + rows <= self.M, "rows out of range")
+        # this rank's output first (local), then the peers
+        order = [self.rank] + [r for r in range(self.world) if r != self.rank]
+        dsts = (C.c_void_p * self.world)(*[self.ptrs[r] + row0 * self.N * 4 for r in order])
+        st = nat.lib().tcg_gemm_s8_multi(A_local.data_ptr(), BT.data_ptr(), dsts, self.world, rows, self.N, K,
+                                         nat.TCG_B_NK, _stream_ptr(A_local))
+        nat.check("PeerGather.gemm_int8", st)
+        dist.all_reduce(self._flag, group=self.group)  # every rank's stores precede every later read
+        return self.C
+
+    def close(self):
+        from . import _native as nat
+        torch.cuda.synchronize(self.device)
+        for base in self._opened:
+            nat.lib().tcg_ipc_close(base)
+        self._opened = []
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()

@@ -36,7 +36,18 @@ def _worker(rank, world, port, q):
         BT = torch.randint(-128, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
         r0, r1 = shard_rows(M, world, rank, align=256)
         C = sharded_gemm_int8(A[r0:r1].contiguous(), BT, gather=True)
-        ok = bool(torch.equal(C, T.gemm_int8(A, BT)))
+        full = T.gemm_int8(A, BT)
+        ok = bool(torch.equal(C, full))
+        # the same gather through the GEMM epilogue over peer memory, twice
+        from tensorcoreptx_b200.dist import PeerGather
+        with PeerGather(M, N, dev) as pg:
+            for _ in range(2):
+                pg.C.fill_(-1)
+                dist.barrier()
+                Cp = pg.gemm_int8(A[r0:r1].contiguous(), BT, r0)
+                torch.cuda.synchronize()
+                ok = ok and bool(torch.equal(Cp, full))
+            dist.barrier()
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, ok, ""))
