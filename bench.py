@@ -420,12 +420,15 @@ def run_ours(args):
 
 def profile_traffic(size, rows):
     """DRAM bytes per launch from the committed ncu capture of this kernel
-    (profiles/gemm_s8_traffic.json, a smaller case): read bytes scaled by
-    the MACs of this launch, write bytes by its outputs.  None when absent."""
+    (profiles/gemm_s8_traffic.json): exact for the captured shape; for other
+    per-rank shapes read bytes are scaled by MACs and write bytes by outputs.
+    None when absent."""
     path = os.path.join(ROOT, "profiles", "gemm_s8_traffic.json")
     try:
         with open(path) as f:
             p = json.load(f)
+        if (rows, size, size) == (p["M"], p["N"], p["K"]):
+            return float(p["dram_read_bytes_per_launch"]) + float(p["dram_write_bytes_per_launch"])
         rd = float(p["dram_read_bytes_per_launch"]) / float(p["macs_per_launch"])
         wr = float(p["dram_write_bytes_per_launch"]) / float(p["outputs_per_launch"])
         return rd * rows * size * size + wr * rows * size

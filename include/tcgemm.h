@@ -135,6 +135,13 @@ tcg_status tcg_gemm_s4_static(const int8_t* A_packed, const int8_t* BT_packed, i
 tcg_status tcg_check_device_error(void* stream, uint64_t* word);
 void tcg_set_wait_timeout_ns(uint64_t ns);
 
+/* Self-test of the failure path: launches a kernel whose bounded waits (the
+ * GEMM's own wait code) watch an mbarrier nothing arrives on; after
+ * timeout_ns they record the failure word (detail low byte 0xFF) and the
+ * kernel returns.  tcg_check_device_error then reports TCG_ERR_TIMEOUT and
+ * the device stays usable.  No counterpart in the reference. */
+tcg_status tcg_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
+
 /* Tile overrides for tuning: the tile width (0 = automatic; else 64, 128 or
  * 256) and the CTA shape (0 = automatic, 1 = single-CTA 128-row tiles,
  * 2 = two-CTA 256-row tiles).  Shapes a precision cannot run fall back to

@@ -37,6 +37,7 @@ SIGNATURES = {
     "tcg_gemm_s4_static": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _p]),
     "tcg_check_device_error": (C.c_int, [_p, C.POINTER(C.c_uint64)]),
     "tcg_set_wait_timeout_ns": (None, [C.c_uint64]),
+    "tcg_selftest_wait_timeout": (C.c_int, [C.c_uint64, _p]),
     "tcg_set_tile_n": (None, [_i]),
     "tcg_set_cta_pair": (None, [_i]),
     "tcg_last_cuda_error": (C.c_int, []),

@@ -513,6 +513,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// Self-test of the bounded waits the GEMM uses: thread 0 (wait_bounded) and
+// warp 1 (wait_bounded_warp) wait on an mbarrier nothing ever arrives on.
+// Each wait gives up after timeout_ns and records the failure word; the
+// kernel then returns normally, leaving the context usable.
+__global__ void wait_selftest_kernel(unsigned long long timeout_ns)
+{
+    __shared__ uint64_t bar;
+    __shared__ uint32_t flag;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        flag = 0u;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    volatile uint32_t* abort_flag = &flag;
+    if (threadIdx.x == 0) {
+        wait_bounded(smem_u32(&bar), 0, abort_flag, timeout_ns, 0xFFu);
+    } else if (threadIdx.x >= 32 && threadIdx.x < 64) {
+        // returns once thread 0 has raised the flag (or on its own expiry)
+        wait_bounded_warp(smem_u32(&bar), 0, abort_flag, timeout_ns, 0xFEu);
+    }
+    __syncthreads();
+}
+
 // Widen packed int4 (two per byte, low nibble first) to int8, 16 packed bytes
 // per thread per step.
 __device__ __forceinline__ void widen_word(uint32_t w, uint32_t& o0, uint32_t& o1)

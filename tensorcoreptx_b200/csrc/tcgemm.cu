@@ -596,6 +596,16 @@ tcg_status tcg_ipc_close(void* base)
     return e == cudaSuccess ? TCG_SUCCESS : cuda_fail(e);
 }
 
+tcg_status tcg_selftest_wait_timeout(uint64_t timeout_ns, void* stream)
+{
+    DeviceState* dev;
+    tcg_status s = device_state(&dev);
+    if (s != TCG_SUCCESS) return s;
+    wait_selftest_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(timeout_ns);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TCG_SUCCESS : cuda_fail(e);
+}
+
 void tcg_set_wait_timeout_ns(uint64_t ns) { g_timeout_ns.store(ns ? ns : 2000000000ull); }
 void tcg_set_tile_n(int bn) { g_force_bn.store(bn); }
 int tcg_last_cuda_error(void) { return t_last_cuda_error; }
