@@ -50,6 +50,7 @@ typedef enum {
 
 typedef enum { TCG_ACC_F32 = 0, TCG_ACC_F16 = 1 } tcg_acc;
 typedef enum { TCG_B_KN = 0, TCG_B_NK = 1 } tcg_b_layout;
+typedef enum { TCG_F8_E4M3 = 0, TCG_F8_E5M2 = 1 } tcg_f8_format;
 
 /* fp16 x fp16 -> fp32 C, fp32 (TCG_ACC_F32) or fp16 (TCG_ACC_F16) accumulation.
  * Replaces fp16 launch_kernel: kernels/fp16_wmma.cu:92-102 (fp32 acc) and
@@ -83,6 +84,12 @@ tcg_status tcg_ipc_handle(const void* ptr, void* handle, size_t* offset);
 tcg_status tcg_ipc_open(const void* handle, void** base);
 tcg_status tcg_ipc_close(void* base);
 
+/* fp8 x fp8 -> fp32 C with fp32 accumulation (tcgen05 kind::f8f6f4), each
+ * operand e4m3 or e5m2 (OCP FP8).  The reference lists FP8 as planned and
+ * never built it (README.md:143-146); same layouts and rules as int8. */
+tcg_status tcg_gemm_f8(const void* A, const void* B, float* C, int M, int N, int K, int batches,
+                       tcg_f8_format a_fmt, tcg_f8_format b_fmt, tcg_b_layout b_layout, void* stream);
+
 /* packed int4 x int4 -> int32, exact; B is always BT (N x K/2 bytes).
  * Replaces int4 launch_kernel: kernels/int4_wmma.cu:148-158,
  * kernels/int4_ptx_mma_k64_x4_x2nontrans_ca.cu:168-178.
@@ -94,6 +101,28 @@ size_t tcg_gemm_s4_workspace_size(int M, int N, int K, int batches);
 tcg_status tcg_gemm_s4(const int8_t* A_packed, const int8_t* BT_packed, int32_t* C,
                        int M, int N, int K, int batches,
                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Fused dequantisation (int8 / int4): C (fp32) = (float)(A x B) * (scale_a *
+ * scale_b), the step the reference performs on the host after the GEMM
+ * (src/data_int8.cu:91-95 dequantize, src/main_int8.cu:170-171).  scale_a and
+ * scale_b are device pointers to one float each (e.g. written by
+ * tcg_quantize_absmax_*); the arithmetic is the reference's, rounding for
+ * rounding.  Other arguments as tcg_gemm_s8 / tcg_gemm_s4. */
+tcg_status tcg_gemm_s8_dequant(const int8_t* A, const int8_t* B, float* C, int M, int N, int K, int batches,
+                               tcg_b_layout b_layout, const float* scale_a, const float* scale_b, void* stream);
+tcg_status tcg_gemm_s4_dequant(const int8_t* A_packed, const int8_t* BT_packed, float* C, int M, int N, int K,
+                               int batches, const float* scale_a, const float* scale_b, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* Per-tensor absmax quantisation on the device, bit-identical to the
+ * reference's quantize_absmax (src/data_int8.cu:74-89: codes in [-127,127],
+ * scale = absmax / 127) and quantize_absmax_int4 (src/data_int4.cu:104-127:
+ * codes in [-7,7] packed two per byte along each row of cols_k values, scale =
+ * absmax / 7).  `scale` is a device float that receives the scale.  src must
+ * be 16-byte aligned, dst and scale 4-byte aligned. */
+tcg_status tcg_quantize_absmax_s8(const float* src, int8_t* dst, size_t n, float* scale, void* stream);
+tcg_status tcg_quantize_absmax_s4(const float* src, int8_t* dst_packed, int rows, int cols_k, float* scale,
+                                  void* stream);
 
 /* Widen packed int4 to int8 (low nibble first), n_packed bytes -> 2*n_packed.
  * The first stage of tcg_gemm_s4, exposed for reuse. */

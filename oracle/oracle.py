@@ -83,6 +83,8 @@ def lib():
                 "oracle_gemm_s4": (None, [_p, _p, _p, _i, _i, _i, _i, _i]),
                 "oracle_gemm_f32": (None, [_p, _p, _p, _i, _i, _i, _i, _i]),
                 "oracle_unpack_s4": (None, [_p, _p, _l]),
+                "oracle_f8_to_f64": (C.c_double, [C.c_uint8, _i]),
+                "oracle_gemm_f8_f64": (None, [_p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _i]),
                 "oracle_quantize_absmax_s8": (C.c_float, [_p, _p, _l]),
                 "oracle_quantize_absmax_s4": (C.c_float, [_p, _p, _i, _i]),
                 "oracle_dequantize": (None, [_p, _p, _l, _f, _f]),
@@ -343,3 +345,16 @@ def ref_gemm_rows(which, A, B, M, N, K, Cout, row0, rows, threads=1):
                C.c_void_p(c0 + r0 * cbytes), n, N, K)
 
     _rows_parallel(run, M, row0, rows, threads)
+
+
+def gemm_f8_f64(A, B, a_fmt=0, b_fmt=0, b_kn=False, row0=0, rows=None, threads=1):
+    """fp64 product of fp8 operands given as uint8 codes (fmt 0 = e4m3,
+    1 = e5m2); B is N x K (b_kn=False) or K x N."""
+    A = np.ascontiguousarray(A, np.uint8)
+    B = np.ascontiguousarray(B, np.uint8)
+    M, K = A.shape
+    N = B.shape[1] if b_kn else B.shape[0]
+    Cm = np.zeros((M, N), np.float64)
+    _rows_parallel(lambda r0, n: lib().oracle_gemm_f8_f64(
+        _ptr(A), _ptr(B), _ptr(Cm), M, N, K, a_fmt, b_fmt, int(b_kn), r0, n), M, row0, rows, threads)
+    return Cm

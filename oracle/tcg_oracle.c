@@ -223,6 +223,45 @@ void oracle_gemm_f16_f64(const uint16_t* A, const uint16_t* B, double* C,
     free(lut);
 }
 
+double oracle_f8_to_f64(uint8_t v, int fmt)
+{
+    const int sign = (v >> 7) & 1;
+    int e, m;
+    double val;
+    if (fmt == 0) { /* e4m3 */
+        e = (v >> 3) & 0xF;
+        m = v & 0x7;
+        if (e == 0xF && m == 0x7)
+            return NAN;
+        val = e == 0 ? ldexp((double)m / 8.0, -6) : ldexp(1.0 + (double)m / 8.0, e - 7);
+    } else { /* e5m2 */
+        e = (v >> 2) & 0x1F;
+        m = v & 0x3;
+        if (e == 0x1F)
+            return m ? NAN : (sign ? -INFINITY : INFINITY);
+        val = e == 0 ? ldexp((double)m / 4.0, -14) : ldexp(1.0 + (double)m / 4.0, e - 15);
+    }
+    return sign ? -val : val;
+}
+
+void oracle_gemm_f8_f64(const uint8_t* A, const uint8_t* B, double* C, int M, int N, int K,
+                        int a_fmt, int b_fmt, int b_kn, int row0, int rows)
+{
+    (void)M;
+    double la[256], lb[256];
+    for (int i = 0; i < 256; ++i) {
+        la[i] = oracle_f8_to_f64((uint8_t)i, a_fmt);
+        lb[i] = oracle_f8_to_f64((uint8_t)i, b_fmt);
+    }
+    for (int m = row0; m < row0 + rows; ++m)
+        for (int n = 0; n < N; ++n) {
+            double acc = 0.0;
+            for (int k = 0; k < K; ++k)
+                acc += la[A[(long)m * K + k]] * lb[b_kn ? B[(long)k * N + n] : B[(long)n * K + k]];
+            C[(long)m * N + n] = acc;
+        }
+}
+
 /* int32 accumulation as in the reference; done in uint32 so that a wrap
  * (impossible for |a|,|b| <= 128 and K <= 2^17) is defined behaviour. */
 void oracle_gemm_s8(const int8_t* A, const int8_t* BT, int32_t* C,

@@ -63,6 +63,14 @@ void oracle_gemm_s4(const int8_t* Ap, const int8_t* BTp, int32_t* C,
 void oracle_gemm_f32(const float* A, const float* BT, float* C,
                      int M, int N, int K, int row0, int rows);
 
+/* fp8 (OCP FP8: e4m3 = bias 7, no infinities, S.1111.111 is NaN;
+ * e5m2 = bias 15, IEEE-style inf/NaN) -> float, exact.  fmt 0 = e4m3, 1 = e5m2.
+ * The reference has no fp8 path; this anchors the fp8 GEMM (its tolerance is
+ * the fp16 one, against this fp64 product). */
+double oracle_f8_to_f64(uint8_t v, int fmt);
+void oracle_gemm_f8_f64(const uint8_t* A, const uint8_t* B, double* C, int M, int N, int K,
+                        int a_fmt, int b_fmt, int b_kn, int row0, int rows);
+
 /* ---- nibble helpers (src/data_int4.cu:10-22) ----------------------------- */
 void oracle_unpack_s4(const int8_t* packed, int8_t* out, long n_packed_bytes);
 

@@ -27,6 +27,7 @@ _p, _i, _sz = C.c_void_p, C.c_int, C.c_size_t
 SIGNATURES = {
     "tcg_gemm_f16": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _i, _i, _p]),
     "tcg_gemm_s8": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _i, _p]),
+    "tcg_gemm_f8": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _p]),
     "tcg_gemm_s8_multi": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _i, _p]),
     "tcg_ipc_handle": (C.c_int, [_p, _p, C.POINTER(C.c_size_t)]),
     "tcg_ipc_open": (C.c_int, [_p, C.POINTER(C.c_void_p)]),
@@ -34,6 +35,10 @@ SIGNATURES = {
     "tcg_gemm_s4_workspace_size": (_sz, [_i, _i, _i, _i]),
     "tcg_gemm_s4": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _p, _sz, _p]),
     "tcg_unpack_s4": (C.c_int, [_p, _p, _sz, _p]),
+    "tcg_gemm_s8_dequant": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _i, _p, _p, _p]),
+    "tcg_gemm_s4_dequant": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _sz, _p]),
+    "tcg_quantize_absmax_s8": (C.c_int, [_p, _p, _sz, _p, _p]),
+    "tcg_quantize_absmax_s4": (C.c_int, [_p, _p, _i, _i, _p, _p]),
     "tcg_gemm_s4_static": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _p]),
     "tcg_check_device_error": (C.c_int, [_p, C.POINTER(C.c_uint64)]),
     "tcg_set_wait_timeout_ns": (None, [C.c_uint64]),

@@ -48,13 +48,16 @@ struct GemmParams {
     int l2_a, l2_b;            // L2 eviction priority of A / B loads (l2_policy), -1 = no hint
     int n_extra;               // further destinations of C (peer GPUs' buffers), <= kMaxExtraDst
     void* extra[7];            // each receives the same tile at the same offset as C
+    uint32_t idesc;            // tcgen05 instruction descriptor (make_idesc)
+    const float* scale_a;      // non-null (int kinds): C = float(acc) * (*scale_a * *scale_b)
+    const float* scale_b;
     int vec_store;             // C rows 16-byte aligned (N % 4 == 0, C aligned)
     unsigned long long timeout_ns;
 };
 
-template <bool kI8, bool kAccF16, bool kBMn, int kBN, int kStages, bool kPair>
+template <int kKind, bool kAccF16, bool kBMn, int kBN, int kStages, bool kPair>
 struct GemmTraits {
-    static constexpr int kElem = kI8 ? 1 : 2;
+    static constexpr int kElem = kKind == kKindF16 ? 2 : 1;
     static constexpr int kBK = kBKBytes / kElem;      // K elements per stage
     static constexpr int kUmmaK = 32 / kElem;         // K per instruction (32 bytes)
     static constexpr int kKSteps = kBK / kUmmaK;      // instructions per stage
@@ -68,8 +71,6 @@ struct GemmTraits {
     // MN-major B arrives as kBRows/kAtomN boxes of kAtomN (128 bytes) x kBK rows.
     static constexpr int kAtomN = kBKBytes / kElem;
     static constexpr int kBoxBytesMn = kBK * kBKBytes;
-    static constexpr uint32_t kIdesc =
-        make_idesc(kI8 ? 2u : (kAccF16 ? 0u : 1u), kI8 ? 1u : 0u, kBMn, kTileM, kBN);
     static constexpr int kEpiArrivals = kPair ? 8 : 4;  // one per epilogue warp (of both CTAs)
     static constexpr int kBarrierBytes = 256;
     static constexpr int kEpiStageBytes = 4 * 32 * 32 * 4;  // a 32 x 32 word tile per epilogue warp
@@ -176,12 +177,12 @@ __device__ __forceinline__ uint32_t num_clusters_x()
 //   tensor memory.  Both CTAs' TMA loads complete on the leader's full
 //   barriers; the leader's commits arrive on both CTAs' empty / tmem-full
 //   barriers; both epilogues release the accumulator on the leader's barrier.
-template <bool kI8, bool kAccF16, bool kBMn, int kBN, int kStages, bool kPair>
+template <int kKind, bool kAccF16, bool kBMn, int kBN, int kStages, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const GemmParams p)
 {
-    using T = GemmTraits<kI8, kAccF16, kBMn, kBN, kStages, kPair>;
+    using T = GemmTraits<kKind, kAccF16, kBMn, kBN, kStages, kPair>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -365,9 +366,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         kBMn ? smem_desc_sw128(b_addr + k * T::kUmmaK * kBKBytes, T::kBoxBytesMn, 1024)
                              : smem_desc_sw128(b_addr + k * 32, 16, 1024);
                     if constexpr (kPair)
-                        umma_pair<kI8>(d_tmem, adesc, bdesc, T::kIdesc, (kb | k) != 0 ? 1u : 0u);
+                        umma_pair<kKind>(d_tmem, adesc, bdesc, p.idesc, (kb | k) != 0 ? 1u : 0u);
                     else
-                        umma<kI8>(d_tmem, adesc, bdesc, T::kIdesc, (kb | k) != 0 ? 1u : 0u);
+                        umma<kKind>(d_tmem, adesc, bdesc, p.idesc, (kb | k) != 0 ? 1u : 0u);
                 }
                 if constexpr (kPair)
                     umma_commit_pair(smem_u32(&empty[stage]), 0x3);
@@ -407,6 +408,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tempty_leader0 = kPair ? mapa_shared(smem_u32(&tempty[0]), 0) : smem_u32(&tempty[0]);
         const int rsub = lane >> 3;  // row within a 4-row group on the way out
         const int csub = lane & 7;   // 16-byte chunk (4 columns) within the 32 columns
+        // dequantising epilogue: the per-tensor scales were produced on the
+        // device by an earlier launch on the same stream
+        const bool dequant = kKind == kKindI8 && p.scale_a != nullptr;
+        const float combined = dequant ? __fmul_rn(*p.scale_a, *p.scale_b) : 0.f;
         int local = 0;
         for (int t = unit; t < num_tiles; t += units, ++local) {
             const int acc = local & 1;
@@ -433,6 +438,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
                         v[j] = __float_as_uint(__half2float(__ushort_as_half(static_cast<unsigned short>(v[j] & 0xFFFFu))));
+                }
+                if (dequant) {  // (float)acc * (scale_a * scale_b), one rounding each
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        v[j] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), combined));
                 }
 #pragma unroll
                 for (int q = 0; q < 8; ++q)

@@ -9,6 +9,11 @@
 
 namespace tcg {
 
+// Operand kinds of the tensor-core mainloop.
+constexpr int kKindF16 = 0;  // fp16 x fp16 (kind::f16)
+constexpr int kKindI8 = 1;   // s8 x s8 -> s32 (kind::i8)
+constexpr int kKindF8 = 2;   // e4m3 / e5m2 -> f32 (kind::f8f6f4)
+
 // ---------------------------------------------------------------- helpers --
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p)
@@ -126,15 +131,22 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // D[tmem] (+)= A[smem] * B[smem]; accumulate != 0 keeps D as an input.
-template <bool kI8>
+template <int kKind>
 __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                     uint32_t accumulate)
+                                 uint32_t accumulate)
 {
-    if constexpr (kI8) {
+    if constexpr (kKind == kKindI8) {
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
             "setp.ne.b32 p, %4, 0;\n\t"
             "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    } else if constexpr (kKind == kKindF8) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
             "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
             : "memory");
     } else {
@@ -247,15 +259,22 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 }
 
 // Pair MMA (M = 256 across the two CTAs), issued by the leader CTA only.
-template <bool kI8>
+template <int kKind>
 __device__ __forceinline__ void umma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate)
+                                      uint32_t accumulate)
 {
-    if constexpr (kI8) {
+    if constexpr (kKind == kKindI8) {
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
             "setp.ne.b32 p, %4, 0;\n\t"
             "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    } else if constexpr (kKind == kKindF8) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
             "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
             : "memory");
     } else {
@@ -301,12 +320,14 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
     return d;
 }
 
-// Instruction descriptor for kind::f16 / kind::i8 (dense, no negation).
-//   c_fmt: 0 = F16, 1 = F32, 2 = S32;  ab_fmt: f16 -> 0 (F16), i8 -> 1 (signed)
-__host__ __device__ constexpr uint32_t make_idesc(uint32_t c_fmt, uint32_t ab_fmt, bool b_mn_major,
-                                                  int m, int n)
+// Instruction descriptor for kind::f16 / kind::i8 / kind::f8f6f4 (dense, no
+// negation, A K-major).
+//   c_fmt: 0 = F16, 1 = F32, 2 = S32
+//   a_fmt / b_fmt: f16 -> 0 (F16); i8 -> 1 (signed); f8 -> 0 (E4M3) or 1 (E5M2)
+__host__ __device__ constexpr uint32_t make_idesc(uint32_t c_fmt, uint32_t a_fmt, uint32_t b_fmt,
+                                                  bool b_mn_major, int m, int n)
 {
-    return (c_fmt << 4) | (ab_fmt << 7) | (ab_fmt << 10) | (0u << 15) |
+    return (c_fmt << 4) | (a_fmt << 7) | (b_fmt << 10) | (0u << 15) |
            (static_cast<uint32_t>(b_mn_major) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
            (static_cast<uint32_t>(m >> 4) << 24);
 }

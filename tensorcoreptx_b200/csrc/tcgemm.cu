@@ -17,6 +17,7 @@
 
 #include "../../include/tcgemm.h"
 #include "tcg_gemm_kernel.cuh"
+#include "tcg_quant.cuh"
 
 namespace {
 
@@ -182,18 +183,31 @@ int choose_group_m(int tile_m, int bn, int units, int tiles_m)
     return g < 1 ? 1 : g;
 }
 
-template <bool kI8, bool kAccF16, bool kBMn, int kBN, bool kPair>
+// Epilogue options: further destinations of C (peer buffers) and the
+// dequantisation scales (device pointers).
+struct EpiArgs {
+    void* const* extra = nullptr;
+    int n_extra = 0;
+    const float* scale_a = nullptr;
+    const float* scale_b = nullptr;
+    uint32_t a_fmt = 0, b_fmt = 0;  // fp8 operand formats (0 = E4M3, 1 = E5M2)
+};
+
+template <int kKind, bool kAccF16, bool kBMn, int kBN, bool kPair>
 tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, int M, int N, int K,
-                       int batches, cudaStream_t st, void* const* extra = nullptr, int n_extra = 0)
+                       int batches, cudaStream_t st, const EpiArgs& epi)
 {
+    void* const* extra = epi.extra;
+    const int n_extra = epi.n_extra;
     constexpr int kStages = kPair ? (kBN == 256 ? 6 : 8) : (kBN == 256 ? 4 : (kBN == 128 ? 6 : 8));
-    using T = GemmTraits<kI8, kAccF16, kBMn, kBN, kStages, kPair>;
-    auto kern = gemm_kernel<kI8, kAccF16, kBMn, kBN, kStages, kPair>;
+    constexpr bool kByte = kKind != kKindF16;
+    using T = GemmTraits<kKind, kAccF16, kBMn, kBN, kStages, kPair>;
+    auto kern = gemm_kernel<kKind, kAccF16, kBMn, kBN, kStages, kPair>;
 
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e);
 
-    const CUtensorMapDataType dt = kI8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const CUtensorMapDataType dt = kByte ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const uint64_t es = T::kElem;
     CUtensorMap mA, mB;
     tcg_status s = encode_3d(&mA, dt, A, K, M, batches, K * es, static_cast<uint64_t>(M) * K * es, T::kBK, kBM);
@@ -216,7 +230,7 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     p.num_kb = (K + T::kBK - 1) / T::kBK;
     p.group_m = choose_group_m(T::kTileM, kBN, kPair ? dev.sms / 2 : dev.sms, p.tiles_m);
     static const int env_kalt = env_int("TCG_K_ALT", 1);
-    p.k_alternate = (kI8 && env_kalt) ? 1 : 0;
+    p.k_alternate = (kKind == kKindI8 && env_kalt) ? 1 : 0;  // integer sums are order-free
     // Optional L2 eviction priorities for the A / B loads (-1 = no hint, the
     // default: on B200 the hinted loads doubled DRAM traffic at 32768^3).
     static const int env_l2a = env_int("TCG_L2_A", -1);
@@ -224,6 +238,14 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     p.l2_a = env_l2a;
     p.l2_b = env_l2b;
     p.n_extra = n_extra;
+    if constexpr (kKind == kKindI8)
+        p.idesc = make_idesc(2u, 1u, 1u, kBMn, T::kTileM, kBN);  // S32 <- s8 x s8
+    else if constexpr (kKind == kKindF8)
+        p.idesc = make_idesc(1u, epi.a_fmt, epi.b_fmt, kBMn, T::kTileM, kBN);  // F32 <- e4m3/e5m2
+    else
+        p.idesc = make_idesc(kAccF16 ? 0u : 1u, 0u, 0u, kBMn, T::kTileM, kBN);  // F32|F16 <- f16
+    p.scale_a = epi.scale_a;
+    p.scale_b = epi.scale_b;
     for (int i = 0; i < kMaxExtraDst; ++i) p.extra[i] = i < n_extra ? extra[i] : nullptr;
     if (n_extra > 0) {  // every destination must take 16-byte stores like C
         for (int i = 0; i < n_extra; ++i)
@@ -280,24 +302,25 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     return TCG_SUCCESS;
 }
 
-template <bool kI8, bool kAccF16, bool kBMn>
+template <int kKind, bool kAccF16, bool kBMn>
 tcg_status dispatch_bn(DeviceState& dev, const void* A, const void* B, void* C, int M, int N, int K,
-                       int batches, cudaStream_t st, void* const* extra = nullptr, int n_extra = 0)
+                       int batches, cudaStream_t st, const EpiArgs& epi = EpiArgs())
 {
-    const TileChoice c = choose_tile(M, N, K, kI8 ? 1 : 2, batches, dev.sms, kI8 && kBMn);
+    constexpr bool kByteMn = kKind != kKindF16 && kBMn;  // MN-major byte operand: 128-column atoms
+    const TileChoice c = choose_tile(M, N, K, kKind == kKindF16 ? 2 : 1, batches, dev.sms, kByteMn);
     if (c.pair) {
         if (c.bn == 128) {
             // an MN-major int8 pair tile needs 128 columns per CTA
-            if constexpr (!(kI8 && kBMn)) return launch_gemm<kI8, kAccF16, kBMn, 128, true>(dev, A, B, C, M, N, K, batches, st, extra, n_extra);
+            if constexpr (!kByteMn) return launch_gemm<kKind, kAccF16, kBMn, 128, true>(dev, A, B, C, M, N, K, batches, st, epi);
         }
-        return launch_gemm<kI8, kAccF16, kBMn, 256, true>(dev, A, B, C, M, N, K, batches, st, extra, n_extra);
+        return launch_gemm<kKind, kAccF16, kBMn, 256, true>(dev, A, B, C, M, N, K, batches, st, epi);
     }
     switch (c.bn) {
     case 64:
-        if constexpr (!(kI8 && kBMn)) return launch_gemm<kI8, kAccF16, kBMn, 64, false>(dev, A, B, C, M, N, K, batches, st, extra, n_extra);
+        if constexpr (!kByteMn) return launch_gemm<kKind, kAccF16, kBMn, 64, false>(dev, A, B, C, M, N, K, batches, st, epi);
         [[fallthrough]];
-    case 128: return launch_gemm<kI8, kAccF16, kBMn, 128, false>(dev, A, B, C, M, N, K, batches, st, extra, n_extra);
-    default: return launch_gemm<kI8, kAccF16, kBMn, 256, false>(dev, A, B, C, M, N, K, batches, st, extra, n_extra);
+    case 128: return launch_gemm<kKind, kAccF16, kBMn, 128, false>(dev, A, B, C, M, N, K, batches, st, epi);
+    default: return launch_gemm<kKind, kAccF16, kBMn, 256, false>(dev, A, B, C, M, N, K, batches, st, epi);
     }
 }
 
@@ -364,10 +387,10 @@ tcg_status tcg_gemm_f16(const void* A, const void* B, float* C, int M, int N, in
     if ((s = device_state(&dev)) != TCG_SUCCESS) return s;
     if ((s = resolve_encode()) != TCG_SUCCESS) return s;
     if (acc == TCG_ACC_F32)
-        return b_layout == TCG_B_KN ? dispatch_bn<false, false, true>(*dev, A, B, C, M, N, K, batches, st)
-                                    : dispatch_bn<false, false, false>(*dev, A, B, C, M, N, K, batches, st);
-    return b_layout == TCG_B_KN ? dispatch_bn<false, true, true>(*dev, A, B, C, M, N, K, batches, st)
-                                : dispatch_bn<false, true, false>(*dev, A, B, C, M, N, K, batches, st);
+        return b_layout == TCG_B_KN ? dispatch_bn<kKindF16, false, true>(*dev, A, B, C, M, N, K, batches, st)
+                                    : dispatch_bn<kKindF16, false, false>(*dev, A, B, C, M, N, K, batches, st);
+    return b_layout == TCG_B_KN ? dispatch_bn<kKindF16, true, true>(*dev, A, B, C, M, N, K, batches, st)
+                                : dispatch_bn<kKindF16, true, false>(*dev, A, B, C, M, N, K, batches, st);
 }
 
 tcg_status tcg_gemm_s8(const int8_t* A, const int8_t* B, int32_t* C, int M, int N, int K, int batches,
@@ -383,8 +406,8 @@ tcg_status tcg_gemm_s8(const int8_t* A, const int8_t* B, int32_t* C, int M, int 
     DeviceState* dev;
     if ((s = device_state(&dev)) != TCG_SUCCESS) return s;
     if ((s = resolve_encode()) != TCG_SUCCESS) return s;
-    return b_layout == TCG_B_KN ? dispatch_bn<true, false, true>(*dev, A, B, C, M, N, K, batches, st)
-                                : dispatch_bn<true, false, false>(*dev, A, B, C, M, N, K, batches, st);
+    return b_layout == TCG_B_KN ? dispatch_bn<kKindI8, false, true>(*dev, A, B, C, M, N, K, batches, st)
+                                : dispatch_bn<kKindI8, false, false>(*dev, A, B, C, M, N, K, batches, st);
 }
 
 tcg_status tcg_gemm_s8_multi(const int8_t* A, const int8_t* B, int32_t* const* C_dst, int n_dst, int M, int N,
@@ -412,10 +435,33 @@ tcg_status tcg_gemm_s8_multi(const int8_t* A, const int8_t* B, int32_t* const* C
     DeviceState* dev;
     if ((s = device_state(&dev)) != TCG_SUCCESS) return s;
     if ((s = resolve_encode()) != TCG_SUCCESS) return s;
-    void* const* extra = reinterpret_cast<void* const*>(C_dst + 1);
-    return b_layout == TCG_B_KN
-               ? dispatch_bn<true, false, true>(*dev, A, B, C_dst[0], M, N, K, 1, st, extra, n_dst - 1)
-               : dispatch_bn<true, false, false>(*dev, A, B, C_dst[0], M, N, K, 1, st, extra, n_dst - 1);
+    EpiArgs epi;
+    epi.extra = reinterpret_cast<void* const*>(C_dst + 1);
+    epi.n_extra = n_dst - 1;
+    return b_layout == TCG_B_KN ? dispatch_bn<kKindI8, false, true>(*dev, A, B, C_dst[0], M, N, K, 1, st, epi)
+                                : dispatch_bn<kKindI8, false, false>(*dev, A, B, C_dst[0], M, N, K, 1, st, epi);
+}
+
+tcg_status tcg_gemm_f8(const void* A, const void* B, float* C, int M, int N, int K, int batches,
+                       tcg_f8_format a_fmt, tcg_f8_format b_fmt, tcg_b_layout b_layout, void* stream)
+{
+    if (b_layout != TCG_B_KN && b_layout != TCG_B_NK) return TCG_ERR_ARG;
+    if ((a_fmt != TCG_F8_E4M3 && a_fmt != TCG_F8_E5M2) || (b_fmt != TCG_F8_E4M3 && b_fmt != TCG_F8_E5M2))
+        return TCG_ERR_ARG;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    bool done;
+    tcg_status s = prologue(A, B, C, M, N, K, batches, st, &done);
+    if (s != TCG_SUCCESS || done) return s;
+    if (K % 16 != 0) return TCG_ERR_SHAPE;
+    if (b_layout == TCG_B_KN && N % 16 != 0) return TCG_ERR_SHAPE;
+    DeviceState* dev;
+    if ((s = device_state(&dev)) != TCG_SUCCESS) return s;
+    if ((s = resolve_encode()) != TCG_SUCCESS) return s;
+    EpiArgs epi;
+    epi.a_fmt = static_cast<uint32_t>(a_fmt);
+    epi.b_fmt = static_cast<uint32_t>(b_fmt);
+    return b_layout == TCG_B_KN ? dispatch_bn<kKindF8, false, true>(*dev, A, B, C, M, N, K, batches, st, epi)
+                                : dispatch_bn<kKindF8, false, false>(*dev, A, B, C, M, N, K, batches, st, epi);
 }
 
 size_t tcg_gemm_s4_workspace_size(int M, int N, int K, int batches)
@@ -424,8 +470,12 @@ size_t tcg_gemm_s4_workspace_size(int M, int N, int K, int batches)
     return round256(static_cast<size_t>(batches) * M * K) + round256(static_cast<size_t>(batches) * N * K);
 }
 
-tcg_status tcg_gemm_s4(const int8_t* A_packed, const int8_t* BT_packed, int32_t* C, int M, int N, int K,
-                       int batches, void* workspace, size_t workspace_bytes, void* stream)
+}  // extern "C"
+
+namespace {
+
+tcg_status gemm_s4_impl(const int8_t* A_packed, const int8_t* BT_packed, void* C, int M, int N, int K, int batches,
+                        void* workspace, size_t workspace_bytes, void* stream, const EpiArgs& epi)
 {
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     bool done;
@@ -466,12 +516,98 @@ tcg_status tcg_gemm_s4(const int8_t* A_packed, const int8_t* BT_packed, int32_t*
     s = launch_unpack(A_packed, a8, static_cast<size_t>(batches) * M * (K / 2), dev->sms, st);
     if (s == TCG_SUCCESS)
         s = launch_unpack(BT_packed, b8, static_cast<size_t>(batches) * N * (K / 2), dev->sms, st);
-    if (s == TCG_SUCCESS) s = dispatch_bn<true, false, false>(*dev, a8, b8, C, M, N, K, batches, st);
+    if (s == TCG_SUCCESS) s = dispatch_bn<kKindI8, false, false>(*dev, a8, b8, C, M, N, K, batches, st, epi);
     if (owned) {
         cudaError_t e = cudaFreeAsync(ws, st);
         if (e != cudaSuccess && s == TCG_SUCCESS) s = cuda_fail(e);
     }
     return s;
+}
+
+}  // namespace
+
+extern "C" {
+
+tcg_status tcg_gemm_s4(const int8_t* A_packed, const int8_t* BT_packed, int32_t* C, int M, int N, int K,
+                       int batches, void* workspace, size_t workspace_bytes, void* stream)
+{
+    return gemm_s4_impl(A_packed, BT_packed, C, M, N, K, batches, workspace, workspace_bytes, stream, EpiArgs());
+}
+
+tcg_status tcg_gemm_s4_dequant(const int8_t* A_packed, const int8_t* BT_packed, float* C, int M, int N, int K,
+                               int batches, const float* scale_a, const float* scale_b, void* workspace,
+                               size_t workspace_bytes, void* stream)
+{
+    if (!scale_a || !scale_b) return TCG_ERR_ARG;
+    EpiArgs epi;
+    epi.scale_a = scale_a;
+    epi.scale_b = scale_b;
+    return gemm_s4_impl(A_packed, BT_packed, C, M, N, K, batches, workspace, workspace_bytes, stream, epi);
+}
+
+tcg_status tcg_gemm_s8_dequant(const int8_t* A, const int8_t* B, float* C, int M, int N, int K, int batches,
+                               tcg_b_layout b_layout, const float* scale_a, const float* scale_b, void* stream)
+{
+    if (b_layout != TCG_B_KN && b_layout != TCG_B_NK) return TCG_ERR_ARG;
+    if (!scale_a || !scale_b) return TCG_ERR_ARG;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    bool done;
+    tcg_status s = prologue(A, B, C, M, N, K, batches, st, &done);
+    if (s != TCG_SUCCESS || done) return s;
+    if (K % 16 != 0) return TCG_ERR_SHAPE;
+    if (b_layout == TCG_B_KN && N % 16 != 0) return TCG_ERR_SHAPE;
+    DeviceState* dev;
+    if ((s = device_state(&dev)) != TCG_SUCCESS) return s;
+    if ((s = resolve_encode()) != TCG_SUCCESS) return s;
+    EpiArgs epi;
+    epi.scale_a = scale_a;
+    epi.scale_b = scale_b;
+    return b_layout == TCG_B_KN ? dispatch_bn<kKindI8, false, true>(*dev, A, B, C, M, N, K, batches, st, epi)
+                                : dispatch_bn<kKindI8, false, false>(*dev, A, B, C, M, N, K, batches, st, epi);
+}
+
+static tcg_status quantize_common(const float* src, int8_t* dst, long long n, long long n_out_units, bool s4,
+                                  float* scale, void* stream)
+{
+    if (n == 0) return TCG_SUCCESS;
+    if (!src || !dst || !scale) return TCG_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(src) & 15u) || (reinterpret_cast<uintptr_t>(dst) & 3u) ||
+        (reinterpret_cast<uintptr_t>(scale) & 3u))
+        return TCG_ERR_ALIGN;
+    DeviceState* dev;
+    tcg_status s = device_state(&dev);
+    if (s != TCG_SUCCESS) return s;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(scale, 0, sizeof(float), st);
+    if (e != cudaSuccess) return cuda_fail(e);
+    const long long cap = static_cast<long long>(dev->sms) * 4;
+    long long blocks = (n / 4 + 255) / 256;
+    blocks = blocks < 1 ? 1 : (blocks > cap ? cap : blocks);
+    absmax_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(src, n, reinterpret_cast<int*>(scale));
+    long long qblocks = (n_out_units + 255) / 256;
+    qblocks = qblocks < 1 ? 1 : (qblocks > cap ? cap : qblocks);
+    if (s4)
+        quantize_s4_kernel<<<static_cast<int>(qblocks), 256, 0, st>>>(src, dst, n_out_units,
+                                                                      reinterpret_cast<const int*>(scale));
+    else
+        quantize_s8_kernel<<<static_cast<int>(qblocks), 256, 0, st>>>(src, dst, n,
+                                                                      reinterpret_cast<const int*>(scale));
+    publish_scale_kernel<<<1, 1, 0, st>>>(scale, s4 ? 7.f : 127.f);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? TCG_SUCCESS : cuda_fail(e);
+}
+
+tcg_status tcg_quantize_absmax_s8(const float* src, int8_t* dst, size_t n, float* scale, void* stream)
+{
+    return quantize_common(src, dst, static_cast<long long>(n), static_cast<long long>(n) / 4, false, scale, stream);
+}
+
+tcg_status tcg_quantize_absmax_s4(const float* src, int8_t* dst_packed, int rows, int cols_k, float* scale,
+                                  void* stream)
+{
+    if (rows < 0 || cols_k < 0 || (cols_k & 1)) return TCG_ERR_SHAPE;
+    const long long n = static_cast<long long>(rows) * cols_k;
+    return quantize_common(src, dst_packed, n, n / 2, true, scale, stream);
 }
 
 }  // extern "C"

@@ -182,3 +182,100 @@ def last_tile_n() -> int:
 def last_tile_m() -> int:
     """Rows of C per tile in the most recent launch: 128 (single CTA) or 256 (pair)."""
     return int(nat.lib().tcg_last_tile_m())
+
+
+# ------------------------------------------------------------- quantisation --
+
+def quantize_absmax_int8(x: torch.Tensor):
+    """Per-tensor absmax quantisation on the device: returns (codes int8 with
+    x's shape, scale as a 1-element float32 device tensor), bit-identical to
+    the reference's quantize_absmax (scale = max|x| / 127, codes rounded half
+    away from zero and clamped to [-127, 127])."""
+    _check(x.is_cuda and x.dtype == torch.float32 and x.is_contiguous(),
+           "x must be a contiguous CUDA float32 tensor")
+    q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    scale = torch.empty(1, dtype=torch.float32, device=x.device)
+    st = nat.lib().tcg_quantize_absmax_s8(x.data_ptr(), q.data_ptr(), x.numel(), scale.data_ptr(),
+                                          _stream_ptr(x))
+    nat.check("quantize_absmax_int8", st)
+    return q, scale
+
+
+def quantize_absmax_int4(x: torch.Tensor):
+    """As quantize_absmax_int8 with scale = max|x| / 7 and codes in [-7, 7]
+    packed two per byte along the last dimension (low nibble = even index),
+    the reference's quantize_absmax_int4: x [rows, k] -> codes [rows, k/2]."""
+    _check(x.is_cuda and x.dtype == torch.float32 and x.is_contiguous() and x.dim() == 2,
+           "x must be a contiguous 2-D CUDA float32 tensor")
+    rows, k = x.shape
+    _check(k % 2 == 0, "x must have an even number of columns")
+    q = torch.empty((rows, k // 2), dtype=torch.int8, device=x.device)
+    scale = torch.empty(1, dtype=torch.float32, device=x.device)
+    st = nat.lib().tcg_quantize_absmax_s4(x.data_ptr(), q.data_ptr(), rows, k, scale.data_ptr(), _stream_ptr(x))
+    nat.check("quantize_absmax_int4", st)
+    return q, scale
+
+
+def gemm_int8_dequant(A: torch.Tensor, BT: torch.Tensor, scale_a: torch.Tensor,
+                      scale_b: torch.Tensor) -> torch.Tensor:
+    """C[M,N] fp32 = (A[M,K] int8 x BT[N,K]^T) * (scale_a * scale_b), the
+    dequantisation fused into the GEMM epilogue; scales are 1-element float32
+    CUDA tensors (e.g. from quantize_absmax_int8)."""
+    _check(A.is_cuda and BT.is_cuda, "A and BT must be CUDA tensors")
+    _check(A.dtype == torch.int8 and BT.dtype == torch.int8, "A and BT must be int8")
+    _check(scale_a.is_cuda and scale_b.is_cuda and scale_a.dtype == torch.float32 and
+           scale_b.dtype == torch.float32, "scales must be float32 CUDA tensors")
+    batches, M, N, K = _dims(A, BT, b_kn=False)
+    _check(K == BT.size(-1), "A cols must equal BT cols (both = K)")
+    _check(A.is_contiguous() and BT.is_contiguous(), "A and BT must be contiguous")
+    C = _out(A, M, N, batches, torch.float32)
+    st = nat.lib().tcg_gemm_s8_dequant(A.data_ptr(), BT.data_ptr(), C.data_ptr(), M, N, K, batches,
+                                       nat.TCG_B_NK, scale_a.data_ptr(), scale_b.data_ptr(), _stream_ptr(A))
+    nat.check("gemm_int8_dequant", st)
+    return C
+
+
+def gemm_int4_dequant(A_packed: torch.Tensor, BT_packed: torch.Tensor, scale_a: torch.Tensor,
+                      scale_b: torch.Tensor) -> torch.Tensor:
+    """As gemm_int8_dequant for packed int4 operands [M, K/2] and [N, K/2]."""
+    _check(A_packed.is_cuda and BT_packed.is_cuda, "A and BT must be CUDA tensors")
+    _check(A_packed.dtype == torch.int8 and BT_packed.dtype == torch.int8, "A and BT must be int8 (packed int4)")
+    _check(scale_a.is_cuda and scale_b.is_cuda and scale_a.dtype == torch.float32 and
+           scale_b.dtype == torch.float32, "scales must be float32 CUDA tensors")
+    batches, M, N, Kh = _dims(A_packed, BT_packed, b_kn=False)
+    _check(Kh == BT_packed.size(-1), "A cols must equal BT cols (both = K/2)")
+    _check(A_packed.is_contiguous() and BT_packed.is_contiguous(), "A and BT must be contiguous")
+    K = 2 * Kh
+    need = nat.lib().tcg_gemm_s4_workspace_size(M, N, K, batches)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=A_packed.device)
+    C = _out(A_packed, M, N, batches, torch.float32)
+    st = nat.lib().tcg_gemm_s4_dequant(A_packed.data_ptr(), BT_packed.data_ptr(), C.data_ptr(), M, N, K,
+                                       batches, scale_a.data_ptr(), scale_b.data_ptr(), ws.data_ptr(),
+                                       ws.numel(), _stream_ptr(A_packed))
+    nat.check("gemm_int4_dequant", st)
+    return C
+
+
+# ----------------------------------------------------------------------- fp8 --
+
+_F8_FORMATS = {torch.float8_e4m3fn: 0, torch.float8_e5m2: 1}
+
+
+def gemm_fp8(A: torch.Tensor, B: torch.Tensor, b_layout: str = "nk") -> torch.Tensor:
+    """C[M,N] fp32 = A[M,K] fp8 x B fp8 with fp32 accumulation on tcgen05
+    (kind::f8f6f4).  Operands are torch.float8_e4m3fn or torch.float8_e5m2
+    (formats may differ); B is [N,K] (b_layout="nk", K contiguous) or [K,N]
+    ("kn")."""
+    _check(A.is_cuda and B.is_cuda, "A and B must be CUDA tensors")
+    _check(A.dtype in _F8_FORMATS and B.dtype in _F8_FORMATS, "A and B must be float8_e4m3fn or float8_e5m2")
+    _check(b_layout in ("nk", "kn"), "b_layout must be 'nk' or 'kn'")
+    b_kn = b_layout == "kn"
+    batches, M, N, K = _dims(A, B, b_kn=b_kn)
+    _check(K == (B.size(-2) if b_kn else B.size(-1)), "A cols must equal K of B")
+    _check(A.is_contiguous() and B.is_contiguous(), "A and B must be contiguous")
+    C = _out(A, M, N, batches, torch.float32)
+    st = nat.lib().tcg_gemm_f8(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, batches,
+                               _F8_FORMATS[A.dtype], _F8_FORMATS[B.dtype],
+                               nat.TCG_B_KN if b_kn else nat.TCG_B_NK, _stream_ptr(A))
+    nat.check("gemm_fp8", st)
+    return C

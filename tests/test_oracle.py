@@ -182,3 +182,13 @@ def test_planted_mistake_is_caught():
 def test_threaded_rows_equal_serial():
     A, BT = O.generate_int8(96, 80, 128)
     assert np.array_equal(O.gemm_s8(A[0], BT[0], threads=5), O.gemm_s8(A[0], BT[0]))
+
+
+def test_f8_decoding_matches_torch():
+    import torch
+    codes = np.arange(256, dtype=np.uint8)
+    for fmt, dt in ((0, torch.float8_e4m3fn), (1, torch.float8_e5m2)):
+        mine = np.array([O.lib().oracle_f8_to_f64(int(c), fmt) for c in codes])
+        ref = torch.from_numpy(codes).view(dt).to(torch.float64).numpy()
+        same = (mine == ref) | (np.isnan(mine) & np.isnan(ref))
+        assert same.all(), (fmt, codes[~same][:5])
