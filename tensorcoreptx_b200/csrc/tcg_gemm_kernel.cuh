@@ -55,19 +55,32 @@ struct GemmParams {
     unsigned long long timeout_ns;
 };
 
-template <int kKind, bool kAccF16, bool kBMn, int kBN, int kStages, bool kPair>
+// Tile shapes: one CTA per 128 x BN tile (single), a 2-CTA cluster per
+// 256 x BN tile (pair, cta_group::2), or one CTA per 256 x BN tile with two
+// 128-row accumulators and no accumulator double buffering (wide).
+constexpr int kShapeSingle = 0;
+constexpr int kShapePair = 1;
+constexpr int kShapeWide = 2;
+
+template <int kKind, bool kAccF16, bool kBMn, int kBN, int kStages, int kShape>
 struct GemmTraits {
+    static constexpr bool kPair = kShape == kShapePair;
+    static constexpr bool kWide = kShape == kShapeWide;
     static constexpr int kElem = kKind == kKindF16 ? 2 : 1;
     static constexpr int kBK = kBKBytes / kElem;      // K elements per stage
     static constexpr int kUmmaK = 32 / kElem;         // K per instruction (32 bytes)
     static constexpr int kKSteps = kBK / kUmmaK;      // instructions per stage
-    static constexpr int kTileM = kPair ? 2 * kBM : kBM;  // rows of C per tile
+    static constexpr int kTileM = kShape == kShapeSingle ? kBM : 2 * kBM;  // rows of C per tile
+    static constexpr int kUmmaM = kPair ? 2 * kBM : kBM;  // M of one MMA: 256 only with cta_group::2
+    static constexpr int kASub = kWide ? 2 : 1;       // 128-row blocks of A per CTA
     static constexpr int kBRows = kPair ? kBN / 2 : kBN;  // B rows (N) held by each CTA
-    static constexpr int kABytes = kBM * kBKBytes;
+    static constexpr int kASubBytes = kBM * kBKBytes;
+    static constexpr int kABytes = kASub * kASubBytes;
     static constexpr int kBBytes = kBRows * kBKBytes;
     static constexpr int kStageBytes = kABytes + kBBytes;       // per CTA
     static constexpr int kTxBytes = kPair ? 2 * kStageBytes : kStageBytes;  // per leader barrier
-    static constexpr int kTmemCols = 2 * kBN;         // two accumulators
+    static constexpr int kAccBufs = kWide ? 1 : 2;    // TMEM accumulator buffers
+    static constexpr int kTmemCols = 2 * kBN;         // (single/pair: 2 buffers; wide: 2 halves)
     // MN-major B arrives as kBRows/kAtomN boxes of kAtomN (128 bytes) x kBK rows.
     static constexpr int kAtomN = kBKBytes / kElem;
     static constexpr int kBoxBytesMn = kBK * kBKBytes;
@@ -81,9 +94,6 @@ struct GemmTraits {
     static_assert(2 * kStages + 5 <= 30, "barrier area");
 };
 
-// Tile t -> (batch, tile-row, tile-col): bands of `group_m` tile-rows, walked
-// column by column, so the units running at one time share a few A panels
-// and a few B panels.
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int& b, int& tm,
                                             int& tn)
 {
@@ -177,12 +187,14 @@ __device__ __forceinline__ uint32_t num_clusters_x()
 //   tensor memory.  Both CTAs' TMA loads complete on the leader's full
 //   barriers; the leader's commits arrive on both CTAs' empty / tmem-full
 //   barriers; both epilogues release the accumulator on the leader's barrier.
-template <int kKind, bool kAccF16, bool kBMn, int kBN, int kStages, bool kPair>
+template <int kKind, bool kAccF16, bool kBMn, int kBN, int kStages, int kShape>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const GemmParams p)
 {
-    using T = GemmTraits<kKind, kAccF16, kBMn, kBN, kStages, kPair>;
+    using T = GemmTraits<kKind, kAccF16, kBMn, kBN, kStages, kShape>;
+    constexpr bool kPair = T::kPair;
+    constexpr bool kWide = T::kWide;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -294,10 +306,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 } else {
                     mbar_arrive_expect_tx(fb_local, T::kTxBytes);
-                    if (hint)
-                        tma_load_3d_hint(a_dst, &tmA, fb_local, kc * T::kBK, a_row, b, pol_a);
-                    else
-                        tma_load_3d(a_dst, &tmA, fb_local, kc * T::kBK, a_row, b);
+#pragma unroll
+                    for (int h = 0; h < T::kASub; ++h) {
+                        if (hint)
+                            tma_load_3d_hint(a_dst + h * T::kASubBytes, &tmA, fb_local, kc * T::kBK, a_row + h * kBM,
+                                             b, pol_a);
+                        else
+                            tma_load_3d(a_dst + h * T::kASubBytes, &tmA, fb_local, kc * T::kBK, a_row + h * kBM, b);
+                    }
                     if constexpr (kBMn) {
 #pragma unroll
                         for (int j = 0; j < T::kBRows / T::kAtomN; ++j) {
@@ -341,15 +357,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool aborted = false;
         int local = 0;
         for (int t = unit; t < num_tiles && !aborted; t += units, ++local) {
-            const int acc = local & 1;
-            const uint32_t acc_phase = (local >> 1) & 1;
+            const int acc = local % T::kAccBufs;
+            const uint32_t acc_phase = (local / T::kAccBufs) & 1;
             if (!wait_bounded(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, p.timeout_ns,
                               (blockIdx.x << 8) | 0x20u | acc)) {
                 aborted = true;
                 break;
             }
             tc_fence_after();
-            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);  // wide: acc == 0
             for (int kb = 0; kb < p.num_kb; ++kb) {
                 if (!wait_bounded(smem_u32(&full[stage]), phase, abort_flag, p.timeout_ns,
                                   (blockIdx.x << 8) | 0x30u | stage)) {
@@ -365,10 +381,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint64_t bdesc =
                         kBMn ? smem_desc_sw128(b_addr + k * T::kUmmaK * kBKBytes, T::kBoxBytesMn, 1024)
                              : smem_desc_sw128(b_addr + k * 32, 16, 1024);
-                    if constexpr (kPair)
+                    if constexpr (kPair) {
                         umma_pair<kKind>(d_tmem, adesc, bdesc, p.idesc, (kb | k) != 0 ? 1u : 0u);
-                    else
+                    } else {
                         umma<kKind>(d_tmem, adesc, bdesc, p.idesc, (kb | k) != 0 ? 1u : 0u);
+                        if constexpr (kWide)  // rows 128..255 of the tile into the second half
+                            umma<kKind>(d_tmem + kBN, smem_desc_sw128(a_addr + T::kASubBytes + k * 32, 16, 1024),
+                                        bdesc, p.idesc, (kb | k) != 0 ? 1u : 0u);
+                    }
                 }
                 if constexpr (kPair)
                     umma_commit_pair(smem_u32(&empty[stage]), 0x3);
@@ -388,9 +408,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // Tail: wait until both accumulators' last use has been released by
         // the epilogue(s), so no release arrives on this CTA after it exits.
-        for (int i = 0; i < 2 && !aborted; ++i, ++local) {
-            if (!wait_bounded(smem_u32(&tempty[local & 1]), ((local >> 1) & 1) ^ 1u, abort_flag, p.timeout_ns,
-                              (blockIdx.x << 8) | 0x60u | (local & 1)))
+        for (int i = 0; i < T::kAccBufs && !aborted; ++i, ++local) {
+            const int acc = local % T::kAccBufs;
+            if (!wait_bounded(smem_u32(&tempty[acc]), ((local / T::kAccBufs) & 1) ^ 1u, abort_flag, p.timeout_ns,
+                              (blockIdx.x << 8) | 0x60u | acc))
                 break;
         }
     } else if (warp >= 2) {
@@ -414,19 +435,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float combined = dequant ? __fmul_rn(*p.scale_a, *p.scale_b) : 0.f;
         int local = 0;
         for (int t = unit; t < num_tiles; t += units, ++local) {
-            const int acc = local & 1;
-            const uint32_t acc_phase = (local >> 1) & 1;
+            const int acc = local % T::kAccBufs;
+            const uint32_t acc_phase = (local / T::kAccBufs) & 1;
             if (!wait_bounded_warp(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.timeout_ns,
                                    (blockIdx.x << 8) | 0x40u | acc))
                 break;
             tc_fence_after();
             int b, tm, tn;
             tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, b, tm, tn);
-            const int row0 = tm * T::kTileM + static_cast<int>(rank) * kBM + quarter * 32;
             const int col0 = tn * kBN;
             const long long cbase = static_cast<long long>(b) * p.batch_stride_c;
+#pragma unroll 1
+            for (int h = 0; h < T::kASub; ++h) {  // wide tiles: the two 128-row halves
+            const int row0 = tm * T::kTileM + static_cast<int>(rank) * kBM + h * kBM + quarter * 32;
             const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                                    static_cast<uint32_t>(acc * kBN);
+                                    static_cast<uint32_t>((acc + h) * kBN);
 #pragma unroll 1
             for (int c = 0; c < kBN; c += 32) {
                 const int col = col0 + c;
@@ -472,6 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 __syncwarp();  // the tile is rewritten by the next 32 columns
+            }
             }
             tc_fence_before();
             __syncwarp();

@@ -113,7 +113,7 @@ tcg_status encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
 // MMAs).  Ties go to the earlier (more efficient) shape.
 struct TileChoice {
     int bn;
-    bool pair;
+    int shape;  // kShapeSingle / kShapePair / kShapeWide
 };
 
 // Environment overrides (read once; the tcg_set_* calls take precedence):
@@ -130,40 +130,46 @@ TileChoice choose_tile(int M, int N, int K, int elem_bytes, int batches, int sms
     static const int env_bn = env_int("TCG_TILE_N");
     static const int env_pair = env_int("TCG_CTA_PAIR");
     const int forced_bn = g_force_bn.load() ? g_force_bn.load() : env_bn;
-    const int forced_pair = g_force_pair.load() ? g_force_pair.load() : env_pair;  // 0 auto, 1 single, 2 pair
+    // 0 auto, 1 single, 2 pair, 3 wide
+    const int forced = g_force_pair.load() ? g_force_pair.load() : env_pair;
     struct Cand {
-        bool pair;
+        int shape;
         int bn;
         double eff;
     };
-    static const Cand cands[] = {{true, 256, 1.00}, {false, 256, 0.87}, {true, 128, 0.72},
-                                 {false, 128, 0.72}, {false, 64, 0.50}};
+    static const Cand cands[] = {{kShapePair, 256, 1.00}, {kShapeSingle, 256, 0.87}, {kShapePair, 128, 0.72},
+                                 {kShapeSingle, 128, 0.72}, {kShapeSingle, 64, 0.50}};
     // Measured on B200: once the operand panels one wave of pair tiles streams
     // (about 4400 rows x K bytes at 256 x 256) no longer fit in L2, pair
     // tiles pull about twice the DRAM bytes of single-CTA tiles and lose to
     // them (int8 32768^3: 59 GB vs 29 GB per launch, 2.2 vs 2.5 POPS
-    // sustained).  Such problems use single-CTA tiles.
+    // sustained).  Such problems use the wide single-CTA 256 x 256 tile
+    // (24.7 GB, 2.75 POPS sustained there), which trades the accumulator
+    // double buffer -- cheap when K is this long -- for pair-like operand
+    // reuse without the cross-SM coupling.
     const double wave_bytes = 4400.0 * static_cast<double>(K) * elem_bytes;
     const long long pair_tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256) * batches;
     const bool pair_thrashes = wave_bytes > 100e6 && pair_tiles >= 4LL * (sms / 2);
-    TileChoice best{256, true};
+    if (forced == 3 || (!forced && !forced_bn && pair_thrashes)) return TileChoice{256, kShapeWide};
+    TileChoice best{256, kShapePair};
     double best_cost = -1.0;
     for (const Cand& c : cands) {
-        if ((forced_pair == 1 && c.pair) || (forced_pair == 2 && !c.pair)) continue;
-        if (!forced_pair && c.pair && pair_thrashes) continue;
+        const bool pair = c.shape == kShapePair;
+        if ((forced == 1 && pair) || (forced == 2 && !pair)) continue;
+        if (!forced && pair && pair_thrashes) continue;
         if (forced_bn && c.bn != forced_bn) continue;
-        if (i8_mn && (c.pair ? c.bn / 2 : c.bn) < 128) continue;  // whole 128-byte atoms
-        const long long tm = (M + (c.pair ? 255 : 127)) / (c.pair ? 256 : 128);
+        if (i8_mn && (pair ? c.bn / 2 : c.bn) < 128) continue;  // whole 128-byte atoms
+        const long long tm = (M + (pair ? 255 : 127)) / (pair ? 256 : 128);
         const long long tiles = tm * ((N + c.bn - 1) / c.bn) * batches;
-        const long long units = c.pair ? sms / 2 : sms;
+        const long long units = pair ? sms / 2 : sms;
         const long long waves = (tiles + units - 1) / units;
         const double cost = static_cast<double>(waves) * c.bn / c.eff;
         if (best_cost < 0 || cost < best_cost) {
-            best = TileChoice{c.bn, c.pair};
+            best = TileChoice{c.bn, c.shape};
             best_cost = cost;
         }
     }
-    if (best_cost < 0) best = TileChoice{forced_bn ? forced_bn : 256, forced_pair != 1};
+    if (best_cost < 0) best = TileChoice{forced_bn ? forced_bn : 256, forced == 1 ? kShapeSingle : kShapePair};
     return best;
 }
 
@@ -193,16 +199,18 @@ struct EpiArgs {
     uint32_t a_fmt = 0, b_fmt = 0;  // fp8 operand formats (0 = E4M3, 1 = E5M2)
 };
 
-template <int kKind, bool kAccF16, bool kBMn, int kBN, bool kPair>
+template <int kKind, bool kAccF16, bool kBMn, int kBN, int kShape>
 tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, int M, int N, int K,
                        int batches, cudaStream_t st, const EpiArgs& epi)
 {
     void* const* extra = epi.extra;
     const int n_extra = epi.n_extra;
-    constexpr int kStages = kPair ? (kBN == 256 ? 6 : 8) : (kBN == 256 ? 4 : (kBN == 128 ? 6 : 8));
+    constexpr bool kPair = kShape == kShapePair;
+    constexpr int kStages = kShape == kShapeWide ? 3
+                            : kPair ? (kBN == 256 ? 6 : 8) : (kBN == 256 ? 4 : (kBN == 128 ? 6 : 8));
     constexpr bool kByte = kKind != kKindF16;
-    using T = GemmTraits<kKind, kAccF16, kBMn, kBN, kStages, kPair>;
-    auto kern = gemm_kernel<kKind, kAccF16, kBMn, kBN, kStages, kPair>;
+    using T = GemmTraits<kKind, kAccF16, kBMn, kBN, kStages, kShape>;
+    auto kern = gemm_kernel<kKind, kAccF16, kBMn, kBN, kStages, kShape>;
 
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e);
@@ -239,11 +247,11 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     p.l2_b = env_l2b;
     p.n_extra = n_extra;
     if constexpr (kKind == kKindI8)
-        p.idesc = make_idesc(2u, 1u, 1u, kBMn, T::kTileM, kBN);  // S32 <- s8 x s8
+        p.idesc = make_idesc(2u, 1u, 1u, kBMn, T::kUmmaM, kBN);  // S32 <- s8 x s8
     else if constexpr (kKind == kKindF8)
-        p.idesc = make_idesc(1u, epi.a_fmt, epi.b_fmt, kBMn, T::kTileM, kBN);  // F32 <- e4m3/e5m2
+        p.idesc = make_idesc(1u, epi.a_fmt, epi.b_fmt, kBMn, T::kUmmaM, kBN);  // F32 <- e4m3/e5m2
     else
-        p.idesc = make_idesc(kAccF16 ? 0u : 1u, 0u, 0u, kBMn, T::kTileM, kBN);  // F32|F16 <- f16
+        p.idesc = make_idesc(kAccF16 ? 0u : 1u, 0u, 0u, kBMn, T::kUmmaM, kBN);  // F32|F16 <- f16
     p.scale_a = epi.scale_a;
     p.scale_b = epi.scale_b;
     for (int i = 0; i < kMaxExtraDst; ++i) p.extra[i] = i < n_extra ? extra[i] : nullptr;
@@ -308,19 +316,20 @@ tcg_status dispatch_bn(DeviceState& dev, const void* A, const void* B, void* C, 
 {
     constexpr bool kByteMn = kKind != kKindF16 && kBMn;  // MN-major byte operand: 128-column atoms
     const TileChoice c = choose_tile(M, N, K, kKind == kKindF16 ? 2 : 1, batches, dev.sms, kByteMn);
-    if (c.pair) {
+    if (c.shape == kShapeWide) return launch_gemm<kKind, kAccF16, kBMn, 256, kShapeWide>(dev, A, B, C, M, N, K, batches, st, epi);
+    if (c.shape == kShapePair) {
         if (c.bn == 128) {
-            // an MN-major int8 pair tile needs 128 columns per CTA
-            if constexpr (!kByteMn) return launch_gemm<kKind, kAccF16, kBMn, 128, true>(dev, A, B, C, M, N, K, batches, st, epi);
+            // an MN-major byte pair tile needs 128 columns per CTA
+            if constexpr (!kByteMn) return launch_gemm<kKind, kAccF16, kBMn, 128, kShapePair>(dev, A, B, C, M, N, K, batches, st, epi);
         }
-        return launch_gemm<kKind, kAccF16, kBMn, 256, true>(dev, A, B, C, M, N, K, batches, st, epi);
+        return launch_gemm<kKind, kAccF16, kBMn, 256, kShapePair>(dev, A, B, C, M, N, K, batches, st, epi);
     }
     switch (c.bn) {
     case 64:
-        if constexpr (!kByteMn) return launch_gemm<kKind, kAccF16, kBMn, 64, false>(dev, A, B, C, M, N, K, batches, st, epi);
+        if constexpr (!kByteMn) return launch_gemm<kKind, kAccF16, kBMn, 64, kShapeSingle>(dev, A, B, C, M, N, K, batches, st, epi);
         [[fallthrough]];
-    case 128: return launch_gemm<kKind, kAccF16, kBMn, 128, false>(dev, A, B, C, M, N, K, batches, st, epi);
-    default: return launch_gemm<kKind, kAccF16, kBMn, 256, false>(dev, A, B, C, M, N, K, batches, st, epi);
+    case 128: return launch_gemm<kKind, kAccF16, kBMn, 128, kShapeSingle>(dev, A, B, C, M, N, K, batches, st, epi);
+    default: return launch_gemm<kKind, kAccF16, kBMn, 256, kShapeSingle>(dev, A, B, C, M, N, K, batches, st, epi);
     }
 }
 

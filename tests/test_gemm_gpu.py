@@ -397,8 +397,9 @@ _SHAPE_CASES = [(1, 300, 528, 384), (2, 260, 144, 128), (1, 512, 1024, 256)]
 
 @pytest.mark.parametrize("prec", ["int8", "int8_kn", "int4", "fp16", "fp16_nk", "fp16acc"])
 def test_every_tile_shape_gives_identical_results(prec):
-    """Single-CTA 128-row tiles (widths 64/128/256) and CTA-pair 256-row tiles
-    (widths 128/256) must all produce the same C: integer results equal the
+    """Single-CTA 128-row tiles (widths 64/128/256), CTA-pair 256-row tiles
+    (widths 128/256) and single-CTA 256 x 256 tiles with two accumulators must
+    all produce the same C: integer results equal the
     oracle, and fp16 results are bit-identical across shapes because every
     element accumulates in the same k order."""
     T = tcg()
@@ -423,14 +424,14 @@ def test_every_tile_shape_gives_identical_results(prec):
                 (lambda: T.gemm_fp16(_cuda(A, torch.float16), _cuda(B, torch.float16), acc=acc))
         outs = {}
         try:
-            for mode, bns in ((1, (64, 128, 256)), (2, (128, 256))):
+            for mode, bns in ((1, (64, 128, 256)), (2, (128, 256)), (3, (256,))):
                 for bn in bns:
                     T.set_cta_pair(mode)
                     T.set_tile_n(bn)
                     outs[(mode, bn)] = fn().cpu().numpy()
                     shape_used = (T.last_tile_m(), T.last_tile_n())
                     if not (prec == "int8_kn" and (mode, bn) in ((1, 64), (2, 128))):
-                        assert shape_used == (128 * mode, bn), (prec, mode, bn, shape_used)
+                        assert shape_used == ((128, 256, 256)[mode - 1], bn), (prec, mode, bn, shape_used)
         finally:
             T.set_cta_pair(0)
             T.set_tile_n(0)
