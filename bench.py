@@ -76,7 +76,9 @@ def load_peaks():
 # ---------------------------------------------------------------- clocks ----
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled every 200 ms."""
+    """nvidia-smi clocks and throttle reasons, sampled every 50 ms, each
+    sample tagged with the bench phase it fell in ("kernel" = the resident
+    timed loop, "e2e" = the end-to-end loop, None = neither)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -87,12 +89,12 @@ class ClockSampler:
         self.rows = []
         self.proc = None
         self.t = None
-        self.active = False
+        self.active = None
 
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", ",".join(str(g) for g in self.gpus)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
@@ -107,8 +109,8 @@ class ClockSampler:
             if len(parts) == 9:
                 self.rows.append((time.time(), self.active, parts))
 
-    def mark(self, active: bool):
-        self.active = active
+    def mark(self, phase):
+        self.active = phase
 
     def stop(self):
         if self.proc is not None:
@@ -120,9 +122,12 @@ class ClockSampler:
         if self.t is not None:
             self.t.join(timeout=5)
 
-    def summary(self):
-        rows = [r for r in self.rows if r[1]] or self.rows
-        window = "timed" if any(r[1] for r in self.rows) else "whole run"
+    def summary(self, phase="kernel"):
+        rows = [r for r in self.rows if r[1] == phase]
+        window = phase
+        if not rows:
+            rows = self.rows
+            window = "whole run"
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"],
                     "samples": 0}
@@ -132,6 +137,7 @@ class ClockSampler:
         reasons = sorted({names[i] for r in rows for i in range(4) if r[2][5 + i] == "Active"})
         pw = [float(r[2][3]) for r in rows if r[2][3].replace(".", "").isdigit()]
         return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_mhz_min": min(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
                 "power_w_max": max(pw) if pw else None, "samples": len(rows), "window": window}
 
@@ -298,7 +304,7 @@ def run_ours(args):
           for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize()
-    clocks.mark(True)
+    clocks.mark("kernel")
     t_begin = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     t_begin.record(stream)
@@ -312,7 +318,7 @@ def run_ours(args):
     t_end.record(stream)
     torch.cuda.synchronize()
     barrier()
-    clocks.mark(False)
+    clocks.mark(None)
     total_ms = max_over_ranks(t_begin.elapsed_time(t_end))
     launch_ms = [a.elapsed_time(b) for a, b in ev]
     kern_ms = max_over_ranks(sum(launch_ms) / len(launch_ms))
@@ -342,7 +348,7 @@ def run_ours(args):
     e2e_steps = max(3, min(args.steps, 10))
     barrier()
     torch.cuda.synchronize()
-    clocks.mark(True)
+    clocks.mark("e2e")
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -352,7 +358,7 @@ def run_ours(args):
         e1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    clocks.mark(False)
+    clocks.mark(None)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
     h2d = rows * size + size * size
     d2h = rows * size * 4
@@ -409,7 +415,8 @@ def run_ours(args):
             "e2e": {"value": ops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": args.steps,
-            "clocks": clocks.summary(),
+            "clocks": clocks.summary("kernel"),
+            "clocks_e2e": clocks.summary("e2e"),
         }
 
     if world > 1:

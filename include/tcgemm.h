@@ -155,6 +155,13 @@ tcg_status tcg_unpack_s4(const int8_t* packed, int8_t* out, size_t n_packed, voi
 tcg_status tcg_gemm_s4_static(const int8_t* A_packed, const int8_t* BT_packed, int32_t* C,
                               int M, int N, int K, int batches, void* stream);
 
+/* Strided 2-D copy (height rows of width_bytes), host<->device or
+ * device<->device, asynchronous on `stream` (cudaMemcpy2DAsync, direction
+ * from the pointers).  Used by the host-buffer GEMM pipeline to move C blocks
+ * between contiguous device buffers and a row-major host matrix. */
+tcg_status tcg_copy_2d_async(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width_bytes,
+                             size_t height, void* stream);
+
 /* Device-side failure word.  Every wait inside the GEMM kernel is bounded
  * (default 2 s, tcg_set_wait_timeout_ns); on expiry the kernel records
  * (code << 32 | detail) here, drains its own copies in flight, frees its

@@ -741,6 +741,16 @@ tcg_status tcg_ipc_close(void* base)
     return e == cudaSuccess ? TCG_SUCCESS : cuda_fail(e);
 }
 
+tcg_status tcg_copy_2d_async(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width_bytes,
+                             size_t height, void* stream)
+{
+    if (height == 0 || width_bytes == 0) return TCG_SUCCESS;
+    if (!dst || !src || dpitch < width_bytes || spitch < width_bytes) return TCG_ERR_ARG;
+    cudaError_t e = cudaMemcpy2DAsync(dst, dpitch, src, spitch, width_bytes, height, cudaMemcpyDefault,
+                                      static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TCG_SUCCESS : cuda_fail(e);
+}
+
 tcg_status tcg_selftest_wait_timeout(uint64_t timeout_ns, void* stream)
 {
     DeviceState* dev;

@@ -2,13 +2,14 @@
 
 The reference copies whole matrices to the device, runs one launch and copies
 C back (src/main_int8.cu:113-122).  Over PCIe the copies dominate: at
-M = N = K = 32768 (int8) the step moves 2 GiB in and 4 GiB out for ~30 ms of
-tensor-core work.  These entry points take pinned host tensors and pipeline
-row chunks of C: while chunk i is multiplied on the caller's current stream,
-the A rows of chunk i+1 are copied in on one stream and C rows of chunk i-1
-copied out on another (B, which every chunk needs in full, goes first).  The
-result lands in a pinned host tensor; like the device entry points, the call
-is asynchronous with respect to the host.
+M = N = K = 32768 (int8) the step moves 2 GiB in and 4 GiB out for ~25 ms of
+tensor-core work.  These entry points take pinned host tensors and split C
+into blocks (row chunks x column chunks): block (i, j) is multiplied on the
+caller's current stream once row chunk i of A and column chunk j of B are on
+the device, while further operand chunks are copied in on one stream and
+finished C blocks copied out (strided, into the row-major host C) on
+another.  The result lands in a pinned host tensor; like the device entry
+points, the call is asynchronous with respect to the host.
 
 Every multiply goes through libtcgemm.so (the C ABI); torch only provides the
 pinned/device buffers, streams and events.
@@ -46,42 +47,84 @@ def _row_chunks(M: int, chunks: int):
     return [(r0, min(M, r0 + rows)) for r0 in range(0, M, rows)]
 
 
-def _pipeline(A_h, B_h, C_h, M, launch, chunks, device):
-    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+def _block_schedule(mc: int, nc: int):
+    """Inbound copies and block multiplies in order of readiness.
+
+    Operand chunks go in alternately (A_0, B_0, A_1, B_1, ...); after each one
+    every block whose two operand chunks are now on the device is multiplied
+    (an "L" of new blocks).  Returns a list of ("a", i), ("b", j) and
+    ("mm", i, j) steps.  The number of ready blocks grows with the square of
+    the chunks copied in, so the outbound copies of finished blocks -- the
+    larger half of the PCIe traffic -- start after one A and one B chunk and
+    then never wait for work.
+    """
+    steps = []
+    for s in range(max(mc, nc)):
+        if s < mc:
+            steps.append(("a", s))
+            steps += [("mm", s, j) for j in range(min(s, nc))]
+        if s < nc:
+            steps.append(("b", s))
+            steps += [("mm", i, s) for i in range(min(s + 1, mc))]
+    return steps
+
+
+def _pipeline2d(M, N, blocks, dev, copy_a, copy_b, launch, copy_c):
+    """Run C = A x B block by block over three streams: inbound copies on one,
+    block multiplies on the caller's current stream (each waits for its two
+    operand chunks), outbound copies of finished blocks on the third, in the
+    order of _block_schedule."""
     cur = torch.cuda.current_stream(dev)
     s_in, s_out = _streams(dev)
-    A_d = torch.empty(A_h.shape, dtype=A_h.dtype, device=dev)
-    B_d = torch.empty(B_h.shape, dtype=B_h.dtype, device=dev)
-    C_d = torch.empty(C_h.shape, dtype=C_h.dtype, device=dev)
+    rows = _row_chunks(M, blocks[0])
+    cols = _row_chunks(N, blocks[1])
     s_in.wait_stream(cur)
     s_out.wait_stream(cur)
-    with torch.cuda.stream(s_in):
-        B_d.copy_(B_h, non_blocking=True)
-    for (r0, r1) in _row_chunks(M, chunks):
-        with torch.cuda.stream(s_in):
-            A_d[r0:r1].copy_(A_h[r0:r1], non_blocking=True)
-            ready = torch.cuda.Event()
-            ready.record(s_in)
-        cur.wait_event(ready)
-        launch(A_d, B_d, C_d, r0, r1, cur)
+    ready = {}
+    waited = set()
+    for step in _block_schedule(len(rows), len(cols)):
+        if step[0] in ("a", "b"):
+            kind, idx = step
+            with torch.cuda.stream(s_in):
+                (copy_a if kind == "a" else copy_b)(*(rows if kind == "a" else cols)[idx], s_in)
+                ev = torch.cuda.Event()
+                ev.record(s_in)
+            ready[(kind, idx)] = ev
+            continue
+        _, i, j = step
+        for key in (("a", i), ("b", j)):
+            if key not in waited:
+                cur.wait_event(ready[key])
+                waited.add(key)
+        (r0, r1), (c0, c1) = rows[i], cols[j]
+        launch(r0, r1, c0, c1, cur)
         done = torch.cuda.Event()
         done.record(cur)
         s_out.wait_event(done)
-        with torch.cuda.stream(s_out):
-            C_h[r0:r1].copy_(C_d[r0:r1], non_blocking=True)
+        copy_c(r0, r1, c0, c1, s_out)
     cur.wait_stream(s_out)
-    # the device buffers were allocated on `cur` and used on the copy streams
-    A_d.record_stream(s_in)
-    B_d.record_stream(s_in)
-    C_d.record_stream(s_out)
-    return C_h
+
+
+def _blocks_for(M, N, chunks):
+    return (max(1, min(chunks, -(-M // 256))), max(1, min(chunks, -(-N // 256))))
+
+
+def _c_block_offsets(M, N, blocks):
+    """Start (elements) of each contiguous device C block, 256-byte aligned."""
+    offs, at = {}, 0
+    for (r0, r1) in _row_chunks(M, blocks[0]):
+        for (c0, c1) in _row_chunks(N, blocks[1]):
+            offs[(r0, c0)] = at
+            at += -(-((r1 - r0) * (c1 - c0)) // 64) * 64
+    return offs, at
 
 
 def gemm_int8_host(A: torch.Tensor, BT: torch.Tensor, out: torch.Tensor | None = None,
                    chunks: int = 8, device=None) -> torch.Tensor:
     """C[M,N] int32 = A[M,K] int8 x BT[N,K]^T int8, all three in (pinned) host
-    memory; the multiply runs on the current CUDA device, overlapped with the
-    copies.  Synchronise the current stream before reading C."""
+    memory; the multiply runs on the current CUDA device in chunks x chunks
+    blocks overlapped with the copies.  Synchronise the current stream before
+    reading C."""
     _check_host(A, "A", torch.int8)
     _check_host(BT, "BT", torch.int8)
     _check(A.size(1) == BT.size(1), "A cols must equal BT cols (both = K)")
@@ -90,13 +133,39 @@ def gemm_int8_host(A: torch.Tensor, BT: torch.Tensor, out: torch.Tensor | None =
     C = out if out is not None else torch.empty((M, N), dtype=torch.int32, pin_memory=True)
     _check_host(C, "out", torch.int32)
     _check(tuple(C.shape) == (M, N), "out must be M x N")
+    if M == 0 or N == 0:
+        return C
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    blocks = _blocks_for(M, N, chunks)
+    offs, c_elems = _c_block_offsets(M, N, blocks)
+    A_d = torch.empty((M, K), dtype=torch.int8, device=dev)
+    B_d = torch.empty((N, K), dtype=torch.int8, device=dev)
+    C_d = torch.empty(max(1, c_elems), dtype=torch.int32, device=dev)
+    L = nat.lib()
 
-    def launch(A_d, B_d, C_d, r0, r1, stream):
-        st = nat.lib().tcg_gemm_s8(A_d.data_ptr() + r0 * K, B_d.data_ptr(), C_d.data_ptr() + r0 * N * 4,
-                                   r1 - r0, N, K, 1, nat.TCG_B_NK, stream.cuda_stream)
+    def copy_a(r0, r1, stream):
+        A_d[r0:r1].copy_(A[r0:r1], non_blocking=True)
+
+    def copy_b(c0, c1, stream):
+        B_d[c0:c1].copy_(BT[c0:c1], non_blocking=True)
+
+    def launch(r0, r1, c0, c1, stream):
+        st = L.tcg_gemm_s8(A_d.data_ptr() + r0 * K, B_d.data_ptr() + c0 * K,
+                           C_d.data_ptr() + offs[(r0, c0)] * 4, r1 - r0, c1 - c0, K, 1, nat.TCG_B_NK,
+                           stream.cuda_stream)
         nat.check("gemm_int8_host", st)
 
-    return _pipeline(A, BT, C, M, launch, chunks, device)
+    def copy_c(r0, r1, c0, c1, stream):
+        st = L.tcg_copy_2d_async(C.data_ptr() + (r0 * N + c0) * 4, N * 4, C_d.data_ptr() + offs[(r0, c0)] * 4,
+                                 (c1 - c0) * 4, (c1 - c0) * 4, r1 - r0, stream.cuda_stream)
+        nat.check("gemm_int8_host", st)
+
+    _pipeline2d(M, N, blocks, dev, copy_a, copy_b, launch, copy_c)
+    s_in, s_out = _streams(dev)
+    A_d.record_stream(s_in)
+    B_d.record_stream(s_in)
+    C_d.record_stream(s_out)
+    return C
 
 
 def gemm_fp16_host(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = None, acc: str = "fp32",
@@ -112,11 +181,44 @@ def gemm_fp16_host(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = 
     C = out if out is not None else torch.empty((M, N), dtype=torch.float32, pin_memory=True)
     _check_host(C, "out", torch.float32)
     _check(tuple(C.shape) == (M, N), "out must be M x N")
+    if M == 0 or N == 0:
+        return C
     mode = nat.TCG_ACC_F32 if acc == "fp32" else nat.TCG_ACC_F16
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    blocks = _blocks_for(M, N, chunks)
+    offs, c_elems = _c_block_offsets(M, N, blocks)
+    A_d = torch.empty((M, K), dtype=torch.float16, device=dev)
+    # B column blocks are stored one after another, each K x cols contiguous
+    b_offs, at = {}, 0
+    for (c0, c1) in _row_chunks(N, blocks[1]):
+        b_offs[c0] = at
+        at += -(-(K * (c1 - c0)) // 128) * 128
+    B_d = torch.empty(max(1, at), dtype=torch.float16, device=dev)
+    C_d = torch.empty(max(1, c_elems), dtype=torch.float32, device=dev)
+    L = nat.lib()
 
-    def launch(A_d, B_d, C_d, r0, r1, stream):
-        st = nat.lib().tcg_gemm_f16(A_d.data_ptr() + r0 * K * 2, B_d.data_ptr(), C_d.data_ptr() + r0 * N * 4,
-                                    r1 - r0, N, K, 1, mode, nat.TCG_B_KN, stream.cuda_stream)
+    def copy_a(r0, r1, stream):
+        A_d[r0:r1].copy_(A[r0:r1], non_blocking=True)
+
+    def copy_b(c0, c1, stream):
+        st = L.tcg_copy_2d_async(B_d.data_ptr() + b_offs[c0] * 2, (c1 - c0) * 2, B.data_ptr() + c0 * 2, N * 2,
+                                 (c1 - c0) * 2, K, stream.cuda_stream)
         nat.check("gemm_fp16_host", st)
 
-    return _pipeline(A, B, C, M, launch, chunks, device)
+    def launch(r0, r1, c0, c1, stream):
+        st = L.tcg_gemm_f16(A_d.data_ptr() + r0 * K * 2, B_d.data_ptr() + b_offs[c0] * 2,
+                            C_d.data_ptr() + offs[(r0, c0)] * 4, r1 - r0, c1 - c0, K, 1, mode, nat.TCG_B_KN,
+                            stream.cuda_stream)
+        nat.check("gemm_fp16_host", st)
+
+    def copy_c(r0, r1, c0, c1, stream):
+        st = L.tcg_copy_2d_async(C.data_ptr() + (r0 * N + c0) * 4, N * 4, C_d.data_ptr() + offs[(r0, c0)] * 4,
+                                 (c1 - c0) * 4, (c1 - c0) * 4, r1 - r0, stream.cuda_stream)
+        nat.check("gemm_fp16_host", st)
+
+    _pipeline2d(M, N, blocks, dev, copy_a, copy_b, launch, copy_c)
+    s_in, s_out = _streams(dev)
+    A_d.record_stream(s_in)
+    B_d.record_stream(s_in)
+    C_d.record_stream(s_out)
+    return C

@@ -94,3 +94,20 @@ def test_host_entry_validation():
     assert _row_chunks(1000, 3) == [(0, 512), (512, 1000)]
     assert _row_chunks(100, 8) == [(0, 100)]
     assert _row_chunks(4096, 8) == [(r, r + 512) for r in range(0, 4096, 512)]
+
+
+def test_host_block_schedule_covers_every_block_once_after_its_operands():
+    from tensorcoreptx_b200.host_gemm import _block_schedule
+    for mc, nc in ((1, 1), (8, 8), (3, 7), (7, 2)):
+        steps = _block_schedule(mc, nc)
+        loaded = set()
+        mms = []
+        for st in steps:
+            if st[0] == "mm":
+                assert ("a", st[1]) in loaded and ("b", st[2]) in loaded
+                mms.append(st[1:])
+            else:
+                loaded.add(st)
+        assert sorted(mms) == [(i, j) for i in range(mc) for j in range(nc)]
+        assert loaded == {("a", i) for i in range(mc)} | {("b", j) for j in range(nc)}
+        assert steps[:3] == [("a", 0), ("b", 0), ("mm", 0, 0)]
