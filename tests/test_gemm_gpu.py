@@ -333,6 +333,8 @@ def test_fp16_sweep(n, acc):
     ref_err = max(float(np.abs(Cr[r].astype(np.float64) - refs[r]).max()) for r in rows)
     _record(f"fp16acc_{n}", {"ours": err, "reference_fp16_ptx_fp16acc": ref_err, "tol": tol})
     assert err <= 1.25 * ref_err, (n, err, ref_err, tol)
+    # in fact bit-identical to the reference's kernel
+    assert np.array_equal(C.view(np.uint32), Cr.view(np.uint32))
 
 
 def test_fp16_batched():

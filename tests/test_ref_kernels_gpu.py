@@ -116,3 +116,29 @@ def test_ours_vs_reference_kernels_speed():
     for k, v in res.items():
         if k.startswith("fp16_4096_") and "_ours_" not in k:
             assert res["fp16_4096_ours_ms"] < v, (k, v)
+
+
+@pytest.mark.parametrize("n", [512, 1024, 4096])
+@pytest.mark.parametrize("acc,name", [("fp32", "fp16_wmma"), ("fp16", "fp16_ptx_fp16acc")])
+def test_fp16_bit_identical_to_reference_kernels(n, acc, name):
+    """Both accumulation modes reproduce the reference's own kernels
+    (recompiled for sm_100a, same GPU, same inputs) bit for bit: each output
+    is accumulated 16 k at a time in increasing k with the same rounding."""
+    _need(name)
+    import tensorcoreptx_b200 as T
+    g = torch.Generator(device=DEV).manual_seed(n)
+    A = (torch.rand(n, n, generator=g, device=DEV) * 2 - 1).half()
+    B = (torch.rand(n, n, generator=g, device=DEV) * 2 - 1).half()
+    ours = T.gemm_fp16(A, B, acc=acc)
+    theirs = RK.run(name, A, B, n, n, n)
+    assert torch.equal(ours.view(torch.int32), theirs.view(torch.int32))
+
+
+@pytest.mark.parametrize("name", ["int8_wmma", "int8_ptx_mma_k32"])
+def test_int8_identical_to_reference_kernels_4096(name):
+    _need(name)
+    import tensorcoreptx_b200 as T
+    g = torch.Generator(device=DEV).manual_seed(1)
+    A = torch.randint(-128, 128, (4096, 4096), generator=g, device=DEV, dtype=torch.int8)
+    BT = torch.randint(-128, 128, (4096, 4096), generator=g, device=DEV, dtype=torch.int8)
+    assert torch.equal(T.gemm_int8(A, BT), RK.run(name, A, BT, 4096, 4096, 4096))
