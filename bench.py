@@ -497,6 +497,28 @@ def extras():
                 out[f"fp16_{n}_torch_matmul"] = {"tflops": 2 * n ** 3 / ms_lib / 1e9, "ms": ms_lib}
             del A, B
     torch.cuda.empty_cache()
+    # the smallest configuration (fp16 512^3) is launch-bound from Python;
+    # its device time, from 20 launches replayed in a CUDA graph
+    n = 512
+    A = (torch.rand(n, n, generator=g, device=dev) * 2 - 1).half()
+    B = (torch.rand(n, n, generator=g, device=dev) * 2 - 1).half()
+    C = torch.empty(n, n, dtype=torch.float32, device=dev)
+    from tensorcoreptx_b200 import _native as nat
+    L = nat.lib()
+    s = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            nat.check("fp16", L.tcg_gemm_f16(A.data_ptr(), B.data_ptr(), C.data_ptr(), n, n, n, 1,
+                                             nat.TCG_ACC_F32, nat.TCG_B_KN, s.cuda_stream))
+    s.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        for _ in range(20):
+            nat.check("fp16", L.tcg_gemm_f16(A.data_ptr(), B.data_ptr(), C.data_ptr(), n, n, n, 1,
+                                             nat.TCG_ACC_F32, nat.TCG_B_KN, s.cuda_stream))
+    ms = time_fn(graph.replay, 20) / 20
+    out["fp16_fp32acc_512_graph"] = {"tflops": 2 * n ** 3 / ms / 1e9, "ms": ms}
+    del graph
     return out
 
 

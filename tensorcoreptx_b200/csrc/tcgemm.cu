@@ -212,8 +212,17 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     using T = GemmTraits<kKind, kAccF16, kBMn, kBN, kStages, kShape>;
     auto kern = gemm_kernel<kKind, kAccF16, kBMn, kBN, kStages, kShape>;
 
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmemBytes);
+    // the shared-memory opt-in once per kernel and device (not on every call,
+    // which also keeps launches legal inside stream capture)
+    static std::atomic<bool> smem_set[kMaxDevices];
+    int dev_id = 0;
+    cudaError_t e = cudaGetDevice(&dev_id);
     if (e != cudaSuccess) return cuda_fail(e);
+    if (!smem_set[dev_id].load(std::memory_order_acquire)) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmemBytes);
+        if (e != cudaSuccess) return cuda_fail(e);
+        smem_set[dev_id].store(true, std::memory_order_release);
+    }
 
     const CUtensorMapDataType dt = kByte ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const uint64_t es = T::kElem;
@@ -281,8 +290,6 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
         cfg.numAttrs = 1;
         // persistent grid: no more pairs than can be resident at once
         static int max_clusters[kMaxDevices] = {0};
-        int dev_id = 0;
-        cudaGetDevice(&dev_id);
         if (max_clusters[dev_id] == 0) {
             int n = 0;
             if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
