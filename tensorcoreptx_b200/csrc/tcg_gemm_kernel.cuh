@@ -52,6 +52,7 @@ struct GemmParams {
     const float* scale_a;      // non-null (int kinds): C = float(acc) * (*scale_a * *scale_b)
     const float* scale_b;
     int vec_store;             // C rows 16-byte aligned (N % 4 == 0, C aligned)
+    int tma_store;             // write C through the tensor map (vec_store and no peer destinations)
     unsigned long long timeout_ns;
 };
 
@@ -86,7 +87,8 @@ struct GemmTraits {
     static constexpr int kBoxBytesMn = kBK * kBKBytes;
     static constexpr int kEpiArrivals = kPair ? 8 : 4;  // one per epilogue warp (of both CTAs)
     static constexpr int kBarrierBytes = 256;
-    static constexpr int kEpiStageBytes = 4 * 32 * 32 * 4;  // a 32 x 32 word tile per epilogue warp
+    // two 32 x 32 word staging tiles (4 KB each) per epilogue warp
+    static constexpr int kEpiStageBytes = 4 * 2 * 32 * 32 * 4;
     static constexpr int kSmemBytes = kStages * kStageBytes + kEpiStageBytes + 1024 + kBarrierBytes;
     static_assert(kBRows % kAtomN == 0 || !kBMn, "MN-major B needs whole 128-byte atoms");
     static_assert(kTmemCols >= 32 && kTmemCols <= 512, "TMEM allocation");
@@ -179,6 +181,45 @@ __device__ __forceinline__ uint32_t num_clusters_x()
     return r;
 }
 
+// Convert 32 accumulator words in place: fp16 accumulators (low halves) to
+// fp32, or int32 to fp32 scaled by the combined dequantisation factor.
+template <bool kAccF16>
+__device__ __forceinline__ void epi_convert(uint32_t (&v)[32], bool dequant, float combined)
+{
+    if constexpr (kAccF16) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            v[j] = __float_as_uint(__half2float(__ushort_as_half(static_cast<unsigned short>(v[j] & 0xFFFFu))));
+    }
+    if (dequant) {  // (float)acc * (scale_a * scale_b), one rounding each
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            v[j] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), combined));
+    }
+}
+
+// One 32 x 32 word block of C (lane i holds row i) out through a TMA store:
+// into a staging tile in the tensor map's 128-byte swizzle (16-byte chunk q
+// of row r at chunk q ^ (r & 7): no bank conflicts), then one bulk store.
+// Two staging tiles per warp alternate; before one is rewritten, the store
+// that last read it (two stores ago) must have finished reading.
+__device__ __forceinline__ void epi_store_tma(const CUtensorMap* tmC, uint32_t* buf, uint32_t buf_s,
+                                              const uint32_t (&v)[32], int lane, int col, int row, int b)
+{
+    if (lane == 0) bulk_wait_group_read<1>();
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<uint4*>(buf + lane * 32 + ((q ^ (lane & 7)) << 2)) =
+            make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_3d(tmC, buf_s, col, row, b);
+        bulk_commit_group();
+    }
+}
+
 // kPair = false: one CTA per 128 x kBN tile, tcgen05 cta_group::1.
 // kPair = true : a cluster of two CTAs per 256 x kBN tile, tcgen05
 //   cta_group::2.  CTA r holds rows [128r, 128r+128) of A and columns
@@ -190,7 +231,7 @@ __device__ __forceinline__ uint32_t num_clusters_x()
 template <int kKind, bool kAccF16, bool kBMn, int kBN, int kStages, int kShape>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const GemmParams p)
+                const __grid_constant__ CUtensorMap tmC, const GemmParams p)
 {
     using T = GemmTraits<kKind, kAccF16, kBMn, kBN, kStages, kShape>;
     constexpr bool kPair = T::kPair;
@@ -416,16 +457,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 2) {
         // ---------------------------------------------------- epilogue ----
-        // Each warp owns 32 rows of the tile (its TMEM lane quarter).  Per 32
-        // columns: tcgen05.ld gives lane i row i; the words go through a
-        // 32 x 32 shared-memory tile (16-byte chunks XOR-swizzled by row, so
-        // neither pass has bank conflicts) and come back as 4 rows x 32
-        // columns per instruction, i.e. every global store instruction writes
-        // four whole 128-byte row segments -- of the local C and, for the
-        // epilogue all-gather, of every peer's C over NVLink.
+        // Each warp owns 32 rows of the tile (its TMEM lane quarter) and
+        // reads them 64 columns per tcgen05 wait (two 32x32b.x32 loads: lane
+        // i gets row i).  With a tensor map for C (the usual case), every
+        // 32 x 32 block goes out as one TMA store from a double-buffered,
+        // swizzled staging tile, so the stores run asynchronously beside the
+        // next loads.  Otherwise (peer destinations for the epilogue
+        // all-gather, or C rows that are not 16-byte aligned) the block goes
+        // through a staging tile with plain stores: 4 rows x 128 bytes per
+        // instruction, to C and to every peer's C over NVLink.
         const int quarter = warp & 3;  // TMEM lanes this warp may read
         uint32_t* Cbits = static_cast<uint32_t*>(p.C);
-        uint32_t* stile = epi_stage + (warp - 2) * 32 * 32;
+        uint32_t* stile = epi_stage + (warp - 2) * 2 * 32 * 32;
+        const uint32_t stile_s = smem_u32(stile);
         const uint32_t tempty_leader0 = kPair ? mapa_shared(smem_u32(&tempty[0]), 0) : smem_u32(&tempty[0]);
         const int rsub = lane >> 3;  // row within a 4-row group on the way out
         const int csub = lane & 7;   // 16-byte chunk (4 columns) within the 32 columns
@@ -433,6 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // device by an earlier launch on the same stream
         const bool dequant = kKind == kKindI8 && p.scale_a != nullptr;
         const float combined = dequant ? __fmul_rn(*p.scale_a, *p.scale_b) : 0.f;
+        uint32_t nstore = 0;  // TMA stores issued by this warp (selects the staging tile)
         int local = 0;
         for (int t = unit; t < num_tiles; t += units, ++local) {
             const int acc = local % T::kAccBufs;
@@ -450,6 +495,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row0 = tm * T::kTileM + static_cast<int>(rank) * kBM + h * kBM + quarter * 32;
             const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                     static_cast<uint32_t>((acc + h) * kBN);
+            if (p.tma_store) {
+                if (row0 >= p.M) continue;  // warp-uniform: all 32 rows below the matrix
+#pragma unroll 1
+                for (int c = 0; c < kBN; c += 64) {
+                    const int col = col0 + c;
+                    if (col >= p.N) break;  // warp-uniform
+                    uint32_t va[32], vb[32];
+                    tmem_ld_32x32b_x32(t_addr + c, va);
+                    tmem_ld_32x32b_x32(t_addr + c + 32, vb);
+                    tmem_ld_wait();
+                    epi_convert<kAccF16>(va, dequant, combined);
+                    epi_convert<kAccF16>(vb, dequant, combined);
+                    epi_store_tma(&tmC, stile + (nstore & 1u) * 1024, stile_s + (nstore & 1u) * 4096, va, lane,
+                                  col, row0, b);
+                    ++nstore;
+                    if (col + 32 < p.N) {
+                        epi_store_tma(&tmC, stile + (nstore & 1u) * 1024, stile_s + (nstore & 1u) * 4096, vb,
+                                      lane, col + 32, row0, b);
+                        ++nstore;
+                    }
+                }
+                continue;
+            }
 #pragma unroll 1
             for (int c = 0; c < kBN; c += 32) {
                 const int col = col0 + c;
@@ -457,16 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(t_addr + c, v);
                 tmem_ld_wait();
-                if constexpr (kAccF16) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        v[j] = __float_as_uint(__half2float(__ushort_as_half(static_cast<unsigned short>(v[j] & 0xFFFFu))));
-                }
-                if (dequant) {  // (float)acc * (scale_a * scale_b), one rounding each
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        v[j] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), combined));
-                }
+                epi_convert<kAccF16>(v, dequant, combined);
 #pragma unroll
                 for (int q = 0; q < 8; ++q)
                     *reinterpret_cast<uint4*>(stile + lane * 32 + ((q ^ (lane & 7)) << 2)) =
@@ -507,6 +566,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive(tb);
             }
         }
+        // the staging tiles are read, and C written, before the CTA exits
+        if (lane == 0 && nstore) bulk_wait_group_all();
+        __syncwarp();
     }
 
     if (p.n_extra > 0) __threadfence_system();  // peer stores performed before the kernel ends

@@ -184,6 +184,38 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// ------------------------------------------------------------ TMA stores --
+
+// Shared -> global tiled store (bulk-group completion).  The box's x
+// coordinate must be 16-byte aligned in global memory; rows and columns
+// outside the tensor are not written.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2)
+{
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(src), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Wait until at most kPending committed store groups still read shared memory.
+template <int kPending>
+__device__ __forceinline__ void bulk_wait_group_read()
+{
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kPending) : "memory");
+}
+
+// Wait until every committed store group has completed.
+__device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA) before a store that reads them.
+__device__ __forceinline__ void fence_proxy_async_smem()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ------------------------------------------------- CTA pairs (clusters) --
 
 __device__ __forceinline__ uint32_t cluster_ctarank()
@@ -201,10 +233,14 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank)
     return r;
 }
 
-// Arrive on an mbarrier that may live in another CTA of the cluster.
+// Arrive on an mbarrier that may live in another CTA of the cluster.  The
+// default (release, CTA-scope) semantics: the arrivals only publish that
+// tensor-memory reads finished (tcgen05.wait::ld + fence::before_thread_sync
+// precede them); a cluster-scope release would also wait for every global
+// store the thread has in flight.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr)
 {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 __device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v)

@@ -118,7 +118,9 @@ struct TileChoice {
 
 // Environment overrides (read once; the tcg_set_* calls take precedence):
 // TCG_TILE_N = 64|128|256, TCG_CTA_PAIR = 1 (single) | 2 (pair),
-// TCG_GROUP_M = band height in tiles, TCG_K_ALT = 0|1.
+// TCG_GROUP_M = band height in tiles, TCG_K_ALT = 0|1, TCG_UNITS = at most
+// this many persistent CTAs (pairs of CTAs for pair tiles), TCG_TMA_STORE = 0
+// (write C with plain stores instead of TMA stores).
 int env_int(const char* name, int dflt = 0)
 {
     const char* v = std::getenv(name);
@@ -264,15 +266,25 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     p.scale_a = epi.scale_a;
     p.scale_b = epi.scale_b;
     for (int i = 0; i < kMaxExtraDst; ++i) p.extra[i] = i < n_extra ? extra[i] : nullptr;
-    if (n_extra > 0) {  // every destination must take 16-byte stores like C
-        for (int i = 0; i < n_extra; ++i)
-            if ((reinterpret_cast<uintptr_t>(extra[i]) & 15u) != 0) p.vec_store = 0;
-    }
     p.vec_store = ((N % 4) == 0 && (reinterpret_cast<uintptr_t>(C) % 16) == 0) ? 1 : 0;
+    for (int i = 0; i < n_extra; ++i)  // every destination must take 16-byte stores like C
+        if ((reinterpret_cast<uintptr_t>(extra[i]) & 15u) != 0) p.vec_store = 0;
+    // C through a tensor map (32 x 32 word boxes, 128-byte swizzle) when its
+    // rows are 16-byte aligned and there are no peer destinations
+    static const int env_tma_store = env_int("TCG_TMA_STORE", 1);
+    p.tma_store = (env_tma_store && p.vec_store && n_extra == 0) ? 1 : 0;
+    CUtensorMap mC;
+    std::memset(&mC, 0, sizeof mC);
+    if (p.tma_store) {
+        s = encode_3d(&mC, CU_TENSOR_MAP_DATA_TYPE_INT32, C, N, M, batches, static_cast<uint64_t>(N) * 4,
+                      static_cast<uint64_t>(M) * N * 4, 32, 32);
+        if (s != TCG_SUCCESS) return s;
+    }
     p.timeout_ns = g_timeout_ns.load();
 
     const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n * batches;
     if (tiles > 0x7fffffffLL) return TCG_ERR_SHAPE;
+    static const int env_units = env_int("TCG_UNITS");  // cap on persistent CTAs (pairs), tuning only
     if constexpr (kPair) {
         const long long pairs = dev.sms / 2;
         cudaLaunchConfig_t cfg;
@@ -298,17 +310,19 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
             }
             max_clusters[dev_id] = n;
         }
-        const long long units = max_clusters[dev_id] < pairs ? max_clusters[dev_id] : pairs;
+        long long units = max_clusters[dev_id] < pairs ? max_clusters[dev_id] : pairs;
+        if (env_units > 0 && env_units < units) units = env_units;
         cfg.gridDim = dim3(static_cast<unsigned>(2 * (tiles < units ? tiles : units)), 1, 1);
         static const int debug = env_int("TCG_DEBUG");
         if (debug)
             std::fprintf(stderr, "tcgemm: pair grid %u (max clusters %d) tile 256x%d stages %d group_m %d kalt %d\n",
                          cfg.gridDim.x, max_clusters[dev_id], kBN, kStages, p.group_m, p.k_alternate);
-        e = cudaLaunchKernelEx(&cfg, kern, mA, mB, p);
+        e = cudaLaunchKernelEx(&cfg, kern, mA, mB, mC, p);
         if (e != cudaSuccess) return cuda_fail(e);
     } else {
-        const int grid = static_cast<int>(tiles < dev.sms ? tiles : dev.sms);
-        kern<<<grid, kThreads, T::kSmemBytes, st>>>(mA, mB, p);
+        int grid = static_cast<int>(tiles < dev.sms ? tiles : dev.sms);
+        if (env_units > 0 && env_units < grid) grid = env_units;
+        kern<<<grid, kThreads, T::kSmemBytes, st>>>(mA, mB, mC, p);
     }
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
