@@ -181,8 +181,8 @@ tcg_status tcg_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
 /* Tile overrides for tuning: the tile width (0 = automatic; else 64, 128 or
  * 256) and the tile shape (0 = automatic, 1 = single-CTA 128-row tiles,
  * 2 = two-CTA 256-row tiles, 3 = single-CTA 256 x 256 tiles with two
- * accumulators).  Shapes a precision cannot run fall back to the nearest
- * valid one. */
+ * accumulators, 4 = two-CTA 512 x 256 tiles, two accumulators per CTA).
+ * Shapes a precision cannot run fall back to the nearest valid one. */
 void tcg_set_tile_n(int bn);
 void tcg_set_cta_pair(int mode);
 

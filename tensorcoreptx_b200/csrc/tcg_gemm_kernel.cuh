@@ -53,27 +53,37 @@ struct GemmParams {
     const float* scale_b;
     int vec_store;             // C rows 16-byte aligned (N % 4 == 0, C aligned)
     int tma_store;             // write C through the tensor map (vec_store and no peer destinations)
+    int split_from;            // work items from here on are column halves of the last tiles
+    uint32_t idesc_half;       // instruction descriptor of a half (N = kBN / 2)
+    int dynamic;               // 1: one cluster per work item, taken over by cluster launch control
+    int wave_units;            // units (CTAs or pairs) resident at once
     unsigned long long timeout_ns;
 };
 
 // Tile shapes: one CTA per 128 x BN tile (single), a 2-CTA cluster per
-// 256 x BN tile (pair, cta_group::2), or one CTA per 256 x BN tile with two
-// 128-row accumulators and no accumulator double buffering (wide).
+// 256 x BN tile (pair, cta_group::2), one CTA per 256 x BN tile with two
+// 128-row accumulators and no accumulator double buffering (wide), or a
+// 2-CTA cluster per 512 x BN tile, each CTA holding 256 rows as two 128-row
+// blocks and two accumulators (pair-wide).  Per MAC, pair and wide tiles
+// stream 3/4 of the operand bytes of a single tile from L2, pair-wide tiles
+// 9/16 (with BN = 256: 64 and 48 bytes per clock per SM at the int8 MMA
+// rate).
 constexpr int kShapeSingle = 0;
 constexpr int kShapePair = 1;
 constexpr int kShapeWide = 2;
+constexpr int kShapePairWide = 3;
 
 template <int kKind, bool kAccF16, bool kBMn, int kBN, int kStages, int kShape>
 struct GemmTraits {
-    static constexpr bool kPair = kShape == kShapePair;
-    static constexpr bool kWide = kShape == kShapeWide;
+    static constexpr bool kPair = kShape == kShapePair || kShape == kShapePairWide;  // cta_group::2
+    static constexpr bool kWide = kShape == kShapeWide || kShape == kShapePairWide;  // two A blocks per CTA
     static constexpr int kElem = kKind == kKindF16 ? 2 : 1;
     static constexpr int kBK = kBKBytes / kElem;      // K elements per stage
     static constexpr int kUmmaK = 32 / kElem;         // K per instruction (32 bytes)
     static constexpr int kKSteps = kBK / kUmmaK;      // instructions per stage
-    static constexpr int kTileM = kShape == kShapeSingle ? kBM : 2 * kBM;  // rows of C per tile
-    static constexpr int kUmmaM = kPair ? 2 * kBM : kBM;  // M of one MMA: 256 only with cta_group::2
     static constexpr int kASub = kWide ? 2 : 1;       // 128-row blocks of A per CTA
+    static constexpr int kTileM = kBM * kASub * (kPair ? 2 : 1);  // rows of C per tile
+    static constexpr int kUmmaM = kPair ? 2 * kBM : kBM;  // M of one MMA: 256 only with cta_group::2
     static constexpr int kBRows = kPair ? kBN / 2 : kBN;  // B rows (N) held by each CTA
     static constexpr int kASubBytes = kBM * kBKBytes;
     static constexpr int kABytes = kASub * kASubBytes;
@@ -86,14 +96,16 @@ struct GemmTraits {
     static constexpr int kAtomN = kBKBytes / kElem;
     static constexpr int kBoxBytesMn = kBK * kBKBytes;
     static constexpr int kEpiArrivals = kPair ? 8 : 4;  // one per epilogue warp (of both CTAs)
-    static constexpr int kBarrierBytes = 256;
+    static constexpr int kRing = 4;                      // work-item ring entries
+    static constexpr int kRingConsumers = kPair ? 10 : 5;  // arrivals per ring entry (see the kernel)
+    static constexpr int kBarrierBytes = 512;
     // two 32 x 32 word staging tiles (4 KB each) per epilogue warp
     static constexpr int kEpiStageBytes = 4 * 2 * 32 * 32 * 4;
     static constexpr int kSmemBytes = kStages * kStageBytes + kEpiStageBytes + 1024 + kBarrierBytes;
     static_assert(kBRows % kAtomN == 0 || !kBMn, "MN-major B needs whole 128-byte atoms");
     static_assert(kTmemCols >= 32 && kTmemCols <= 512, "TMEM allocation");
     static_assert(kSmemBytes <= 232448, "shared memory per CTA");
-    static_assert(2 * kStages + 5 <= 30, "barrier area");
+    static_assert(8 * (2 * kStages + 6 + 2 * kRing) + 8 + 4 * kRing <= 384, "barrier area");
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int& b, int& tm,
@@ -111,6 +123,22 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
     tn = rr / gsz;
 }
 
+// Work item -> tile.  Items below split_from are whole tiles; from there on
+// each remaining tile is cut into two column halves, consecutive items, so
+// the last, partial wave of tiles becomes about half as long.
+__device__ __forceinline__ void work_coords(int w, int split_from, int tiles_m, int tiles_n, int group_m, int& b,
+                                            int& tm, int& tn, int& half)
+{
+    int t = w;
+    half = -1;
+    if (w >= split_from) {
+        const int r = w - split_from;
+        t = split_from + (r >> 1);
+        half = r & 1;
+    }
+    tile_coords(t, tiles_m, tiles_n, group_m, b, tm, tn);
+}
+
 __device__ __forceinline__ void record_failure(volatile uint32_t* abort_flag, uint32_t detail)
 {
     *abort_flag = 1u;
@@ -121,13 +149,20 @@ __device__ __forceinline__ void record_failure(volatile uint32_t* abort_flag, ui
 
 // Single-thread bounded wait.  true: the phase of `parity` completed.
 // false: this CTA is aborting (this wait expired, or another role's did).
+template <bool kClusterScope = false>
+__device__ __forceinline__ bool try_wait_scoped(uint32_t bar, uint32_t parity)
+{
+    return kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+}
+
+template <bool kClusterScope = false>
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
                                              unsigned long long timeout_ns, uint32_t detail)
 {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (try_wait_scoped<kClusterScope>(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (try_wait_scoped<kClusterScope>(bar, parity)) return true;
         if (*abort_flag) return false;
         if (global_timer_ns() - t0 > timeout_ns) {
             record_failure(abort_flag, detail);
@@ -139,12 +174,13 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, vola
 // Whole-warp bounded wait with a warp-uniform result.  A completed phase is
 // sticky until every waiter has arrived for the next one, so once any lane
 // sees completion all lanes will.
+template <bool kClusterScope = false>
 __device__ __forceinline__ bool wait_bounded_warp(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
                                                   unsigned long long timeout_ns, uint32_t detail)
 {
     uint64_t t0 = 0;
     for (uint32_t i = 0;; ++i) {
-        const bool ok = mbar_try_wait(bar, parity);
+        const bool ok = try_wait_scoped<kClusterScope>(bar, parity);
         if (__all_sync(0xffffffffu, ok)) return true;
         if (__any_sync(0xffffffffu, ok)) continue;
         if (i == 0) t0 = global_timer_ns();
@@ -231,7 +267,8 @@ __device__ __forceinline__ void epi_store_tma(const CUtensorMap* tmC, uint32_t* 
 template <int kKind, bool kAccF16, bool kBMn, int kBN, int kStages, int kShape>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmC, const GemmParams p)
+                const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmC,
+                const GemmParams p)
 {
     using T = GemmTraits<kKind, kAccF16, kBMn, kBN, kStages, kShape>;
     constexpr bool kPair = T::kPair;
@@ -246,13 +283,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tfull = bars + 2 * kStages;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* qfull = drain + 1;          // work-item ring: entry published
+    uint64_t* qempty = qfull + T::kRing;  // work-item ring: entry read by every consumer (leader CTA's)
+    uint64_t* clcbar = qempty + T::kRing; // cluster launch control response landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(clcbar + 1);
     volatile uint32_t* abort_flag = tmem_slot + 1;
+    volatile int* ring = reinterpret_cast<volatile int*>(tmem_slot + 2);
+    const uint32_t clc_resp = smem_u32(reinterpret_cast<uint8_t*>(bars) + 384);  // 16 bytes, 16-aligned
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const uint32_t rank = kPair ? cluster_ctarank() : 0u;
     const bool leader = (rank == 0u);
+    // this unit's first work item: its own index (one cluster per work item
+    // with cluster launch control, one per resident unit otherwise)
     const int unit = kPair ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
     const int units = kPair ? static_cast<int>(num_clusters_x()) : static_cast<int>(gridDim.x);
 
@@ -266,6 +310,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&tempty[a]), T::kEpiArrivals);
         }
         mbar_init(smem_u32(drain), 1);
+        for (int r = 0; r < T::kRing; ++r) {
+            mbar_init(smem_u32(&qfull[r]), 1);
+            mbar_init(smem_u32(&qempty[r]), T::kRingConsumers);
+        }
+        mbar_init(smem_u32(clcbar), 1);
         *abort_flag = 0u;
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
@@ -287,10 +336,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     const int num_tiles = p.tiles_m * p.tiles_n * p.batches;
+    const int num_work = p.split_from + 2 * (num_tiles - p.split_from);
     const uint32_t stage0 = smem_u32(smem);
     // producer bookkeeping for the abort drain: per stage, a load was issued /
-    // the parity of its phase
+    // the parity of its phase; a cluster-launch-control response in flight
     uint32_t issued = 0, issued_parity = 0;
+    bool clc_pending = false;
+    uint32_t clc_phase = 0;
+
+    // Work items reach every role through a ring of kRing entries in shared
+    // memory.  Thread 0 of the leader CTA (the scheduler) publishes each item
+    // -- into both CTAs' rings for a pair -- and -1 after the last; the
+    // consumers (the MMA issuer, every epilogue warp, and a pair's second
+    // producer) each arrive on the leader's entry-empty barrier once they
+    // have read it.
+    int q = 0;
+    uint32_t qph = 0;
+    const auto ring_next = [&]() {
+        if (++q == T::kRing) {
+            q = 0;
+            qph ^= 1u;
+        }
+    };
+    // a consumer has read entry q: release it on the leader's barrier
+    const auto ring_release = [&]() {
+        if constexpr (kPair) {
+            if (leader)
+                mbar_arrive(smem_u32(&qempty[q]));
+            else
+                mbar_arrive_cluster_release(mapa_shared(smem_u32(&qempty[q]), 0));
+        } else {
+            mbar_arrive(smem_u32(&qempty[q]));
+        }
+    };
 
     if (threadIdx.x == 0) {
         // ------------------------------------------------ TMA producer ----
@@ -301,17 +379,57 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool hint = p.l2_a >= 0 || p.l2_b >= 0;
         const uint64_t pol_a = l2_policy(p.l2_a);
         const uint64_t pol_b = l2_policy(p.l2_b);
-        for (int t = unit; t < num_tiles && !aborted; t += units, ++local) {
-            int b, tm, tn;
-            tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, b, tm, tn);
-            const int a_row = tm * T::kTileM + static_cast<int>(rank) * kBM;
-            const int b_row = tn * kBN + static_cast<int>(rank) * T::kBRows;
+        bool clc_live = p.dynamic != 0;  // the grid may still hold clusters to take over
+        int t = unit;
+        for (;; ++local) {
+            if (leader) {
+                // publish t (scheduler)
+                if (!wait_bounded(smem_u32(&qempty[q]), qph ^ 1u, abort_flag, p.timeout_ns,
+                                  (blockIdx.x << 8) | 0x70u | q)) {
+                    aborted = true;
+                    break;
+                }
+                ring[q] = t;
+                if constexpr (kPair) {
+                    st_cluster_u32(mapa_shared(smem_u32((const void*)&ring[q]), 1), static_cast<uint32_t>(t));
+                    mbar_arrive_cluster_release(mapa_shared(smem_u32(&qfull[q]), 1));
+                }
+                mbar_arrive(smem_u32(&qfull[q]));
+                ring_next();
+                if (t < 0) break;
+                if (clc_live) {  // ask for the next work item now; the answer is read after this tile's loads
+                    mbar_arrive_expect_tx(smem_u32(clcbar), 16);
+                    clc_try_cancel(clc_resp, smem_u32(clcbar));
+                    clc_pending = true;
+                }
+            } else {
+                // a pair's second producer follows the leader's ring
+                if (!wait_bounded<true>(smem_u32(&qfull[q]), qph, abort_flag, p.timeout_ns,
+                                        (blockIdx.x << 8) | 0x78u | q)) {
+                    aborted = true;
+                    break;
+                }
+                t = ring[q];
+                ring_release();
+                ring_next();
+                if (t < 0) break;
+            }
+            int b, tm, tn, half;
+            work_coords(t, p.split_from, p.tiles_m, p.tiles_n, p.group_m, b, tm, tn, half);
+            const int a_row = tm * T::kTileM + static_cast<int>(rank) * (T::kASub * kBM);
+            // a half tile: columns [half * kBN/2, +kBN/2) of the tile, each
+            // CTA of a pair holding half of those
+            const int b_row = half < 0 ? tn * kBN + static_cast<int>(rank) * T::kBRows
+                                       : tn * kBN + half * (kBN / 2) + static_cast<int>(rank) * (T::kBRows / 2);
+            const uint32_t tx = half < 0 ? T::kTxBytes : T::kTxBytes - (kPair ? 2 : 1) * (T::kBBytes / 2);
+            const int b_atoms = half < 0 ? T::kBRows / T::kAtomN : T::kBRows / T::kAtomN / 2;
+            const CUtensorMap* mapB = half < 0 ? &tmB : &tmBh;
             // Units advance through their tiles in step, so the whole grid
             // finishes a wave of tiles at about the same K.  Walking K
             // backwards on every other wave starts each wave on the K range
             // the previous wave just brought into L2.  Integer accumulation is
             // exact in any order; floating-point kinds keep one order.
-            const bool reverse = p.k_alternate && (local & 1);
+            const bool reverse = p.k_alternate && ((t / p.wave_units) & 1);
             for (int kb = 0; kb < p.num_kb; ++kb) {
                 const int kc = reverse ? p.num_kb - 1 - kb : kb;
                 const uint32_t fb_local = smem_u32(&full[stage]);
@@ -324,14 +442,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t b_dst = a_dst + T::kABytes;
                 if constexpr (kPair) {
                     const uint32_t fb = mapa_shared(fb_local, 0);  // the leader's full barrier
-                    if (leader) mbar_arrive_expect_tx(fb_local, T::kTxBytes);
-                    if (hint)
-                        tma_load_3d_pair_hint(a_dst, &tmA, fb, kc * T::kBK, a_row, b, pol_a);
-                    else
-                        tma_load_3d_pair(a_dst, &tmA, fb, kc * T::kBK, a_row, b);
-                    if constexpr (kBMn) {
+                    if (leader) mbar_arrive_expect_tx(fb_local, tx);
 #pragma unroll
-                        for (int j = 0; j < T::kBRows / T::kAtomN; ++j) {
+                    for (int h = 0; h < T::kASub; ++h) {
+                        if (hint)
+                            tma_load_3d_pair_hint(a_dst + h * T::kASubBytes, &tmA, fb, kc * T::kBK, a_row + h * kBM,
+                                                  b, pol_a);
+                        else
+                            tma_load_3d_pair(a_dst + h * T::kASubBytes, &tmA, fb, kc * T::kBK, a_row + h * kBM, b);
+                    }
+                    if constexpr (kBMn) {
+#pragma unroll 1
+                        for (int j = 0; j < b_atoms; ++j) {
                             if (hint)
                                 tma_load_3d_pair_hint(b_dst + j * T::kBoxBytesMn, &tmB, fb,
                                                       b_row + j * T::kAtomN, kc * T::kBK, b, pol_b);
@@ -341,12 +463,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     } else {
                         if (hint)
-                            tma_load_3d_pair_hint(b_dst, &tmB, fb, kc * T::kBK, b_row, b, pol_b);
+                            tma_load_3d_pair_hint(b_dst, mapB, fb, kc * T::kBK, b_row, b, pol_b);
                         else
-                            tma_load_3d_pair(b_dst, &tmB, fb, kc * T::kBK, b_row, b);
+                            tma_load_3d_pair(b_dst, mapB, fb, kc * T::kBK, b_row, b);
                     }
                 } else {
-                    mbar_arrive_expect_tx(fb_local, T::kTxBytes);
+                    mbar_arrive_expect_tx(fb_local, tx);
 #pragma unroll
                     for (int h = 0; h < T::kASub; ++h) {
                         if (hint)
@@ -356,8 +478,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tma_load_3d(a_dst + h * T::kASubBytes, &tmA, fb_local, kc * T::kBK, a_row + h * kBM, b);
                     }
                     if constexpr (kBMn) {
-#pragma unroll
-                        for (int j = 0; j < T::kBRows / T::kAtomN; ++j) {
+#pragma unroll 1
+                        for (int j = 0; j < b_atoms; ++j) {
                             if (hint)
                                 tma_load_3d_hint(b_dst + j * T::kBoxBytesMn, &tmB, fb_local,
                                                  b_row + j * T::kAtomN, kc * T::kBK, b, pol_b);
@@ -367,9 +489,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     } else {
                         if (hint)
-                            tma_load_3d_hint(b_dst, &tmB, fb_local, kc * T::kBK, b_row, b, pol_b);
+                            tma_load_3d_hint(b_dst, mapB, fb_local, kc * T::kBK, b_row, b, pol_b);
                         else
-                            tma_load_3d(b_dst, &tmB, fb_local, kc * T::kBK, b_row, b);
+                            tma_load_3d(b_dst, mapB, fb_local, kc * T::kBK, b_row, b);
                     }
                 }
                 issued |= 1u << stage;
@@ -377,6 +499,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (++stage == kStages) {
                     stage = 0;
                     phase ^= 1u;
+                }
+            }
+            if (aborted) break;
+            if (leader) {  // the next work item
+                if (p.dynamic) {
+                    int next = -1;
+                    if (clc_pending) {
+                        if (!wait_bounded(smem_u32(clcbar), clc_phase, abort_flag, p.timeout_ns,
+                                          (blockIdx.x << 8) | 0x7Cu)) {
+                            aborted = true;
+                            break;
+                        }
+                        clc_pending = false;
+                        clc_phase ^= 1u;
+                        int first_cta;
+                        if (clc_query(clc_resp, first_cta))
+                            next = kPair ? first_cta / 2 : first_cta;
+                        else
+                            clc_live = false;  // nothing left to take over; never ask again
+                    }
+                    t = next;
+                } else {
+                    t = t + units < num_work ? t + units : -1;
                 }
             }
         }
@@ -397,7 +542,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t phase = 0;
         bool aborted = false;
         int local = 0;
-        for (int t = unit; t < num_tiles && !aborted; t += units, ++local) {
+        for (;; ++local) {
+            if (!wait_bounded(smem_u32(&qfull[q]), qph, abort_flag, p.timeout_ns, (blockIdx.x << 8) | 0x74u | q)) {
+                aborted = true;
+                break;
+            }
+            const int t = ring[q];
+            ring_release();
+            ring_next();
+            if (t < 0) break;
+            const uint32_t idesc = t < p.split_from ? p.idesc : p.idesc_half;
             const int acc = local % T::kAccBufs;
             const uint32_t acc_phase = (local / T::kAccBufs) & 1;
             if (!wait_bounded(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, p.timeout_ns,
@@ -423,12 +577,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                         kBMn ? smem_desc_sw128(b_addr + k * T::kUmmaK * kBKBytes, T::kBoxBytesMn, 1024)
                              : smem_desc_sw128(b_addr + k * 32, 16, 1024);
                     if constexpr (kPair) {
-                        umma_pair<kKind>(d_tmem, adesc, bdesc, p.idesc, (kb | k) != 0 ? 1u : 0u);
+                        umma_pair<kKind>(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+                        if constexpr (kWide)  // each CTA's rows 128..255 into the second accumulator
+                            umma_pair<kKind>(d_tmem + kBN,
+                                             smem_desc_sw128(a_addr + T::kASubBytes + k * 32, 16, 1024), bdesc,
+                                             idesc, (kb | k) != 0 ? 1u : 0u);
                     } else {
-                        umma<kKind>(d_tmem, adesc, bdesc, p.idesc, (kb | k) != 0 ? 1u : 0u);
+                        umma<kKind>(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
                         if constexpr (kWide)  // rows 128..255 of the tile into the second half
                             umma<kKind>(d_tmem + kBN, smem_desc_sw128(a_addr + T::kASubBytes + k * 32, 16, 1024),
-                                        bdesc, p.idesc, (kb | k) != 0 ? 1u : 0u);
+                                        bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
                     }
                 }
                 if constexpr (kPair)
@@ -440,12 +598,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     phase ^= 1u;
                 }
             }
-            if (!aborted) {
-                if constexpr (kPair)
-                    umma_commit_pair(smem_u32(&tfull[acc]), 0x3);
-                else
-                    umma_commit(smem_u32(&tfull[acc]));
-            }
+            if (aborted) break;
+            if constexpr (kPair)
+                umma_commit_pair(smem_u32(&tfull[acc]), 0x3);
+            else
+                umma_commit(smem_u32(&tfull[acc]));
         }
         // Tail: wait until both accumulators' last use has been released by
         // the epilogue(s), so no release arrives on this CTA after it exits.
@@ -479,26 +636,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float combined = dequant ? __fmul_rn(*p.scale_a, *p.scale_b) : 0.f;
         uint32_t nstore = 0;  // TMA stores issued by this warp (selects the staging tile)
         int local = 0;
-        for (int t = unit; t < num_tiles; t += units, ++local) {
+        for (;; ++local) {
+            if (!wait_bounded_warp<kPair>(smem_u32(&qfull[q]), qph, abort_flag, p.timeout_ns,
+                                          (blockIdx.x << 8) | 0x7Au | q))
+                break;
+            const int t = ring[q];
+            __syncwarp();
+            if (lane == 0) ring_release();
+            ring_next();
+            if (t < 0) break;
             const int acc = local % T::kAccBufs;
             const uint32_t acc_phase = (local / T::kAccBufs) & 1;
             if (!wait_bounded_warp(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.timeout_ns,
                                    (blockIdx.x << 8) | 0x40u | acc))
                 break;
             tc_fence_after();
-            int b, tm, tn;
-            tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, b, tm, tn);
-            const int col0 = tn * kBN;
+            int b, tm, tn, half;
+            work_coords(t, p.split_from, p.tiles_m, p.tiles_n, p.group_m, b, tm, tn, half);
+            const int col0 = tn * kBN + (half < 0 ? 0 : half * (kBN / 2));
+            const int ncols = half < 0 ? kBN : kBN / 2;
             const long long cbase = static_cast<long long>(b) * p.batch_stride_c;
 #pragma unroll 1
             for (int h = 0; h < T::kASub; ++h) {  // wide tiles: the two 128-row halves
-            const int row0 = tm * T::kTileM + static_cast<int>(rank) * kBM + h * kBM + quarter * 32;
+            const int row0 =
+                tm * T::kTileM + static_cast<int>(rank) * (T::kASub * kBM) + h * kBM + quarter * 32;
             const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                     static_cast<uint32_t>((acc + h) * kBN);
             if (p.tma_store) {
                 if (row0 >= p.M) continue;  // warp-uniform: all 32 rows below the matrix
 #pragma unroll 1
-                for (int c = 0; c < kBN; c += 64) {
+                for (int c = 0; c < ncols; c += 64) {
                     const int col = col0 + c;
                     if (col >= p.N) break;  // warp-uniform
                     uint32_t va[32], vb[32];
@@ -510,7 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     epi_store_tma(&tmC, stile + (nstore & 1u) * 1024, stile_s + (nstore & 1u) * 4096, va, lane,
                                   col, row0, b);
                     ++nstore;
-                    if (col + 32 < p.N) {
+                    if (c + 32 < ncols && col + 32 < p.N) {
                         epi_store_tma(&tmC, stile + (nstore & 1u) * 1024, stile_s + (nstore & 1u) * 4096, vb,
                                       lane, col + 32, row0, b);
                         ++nstore;
@@ -519,7 +686,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 continue;
             }
 #pragma unroll 1
-            for (int c = 0; c < kBN; c += 32) {
+            for (int c = 0; c < ncols; c += 32) {
                 const int col = col0 + c;
                 if (col >= p.N) break;  // warp-uniform
                 uint32_t v[32];
@@ -589,7 +756,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 while (global_timer_ns() - t0 < 2000000ull) {
                 }
             }
-        } else if (threadIdx.x == 32 && leader) {
+        }
+        if (threadIdx.x == 0 && clc_pending) drain_wait(smem_u32(clcbar), clc_phase);  // response in flight
+        if (threadIdx.x == 32 && leader) {
             if constexpr (kPair)
                 umma_commit_pair_local(smem_u32(drain));
             else

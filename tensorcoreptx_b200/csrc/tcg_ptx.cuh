@@ -64,6 +64,54 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
     return ok != 0;
 }
 
+// The same with cluster-scope acquire: for data another CTA of the cluster
+// wrote into this CTA's shared memory before arriving (release, cluster).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// ------------------------------------------------- cluster launch control --
+
+// Ask the hardware to cancel the launch of a cluster of this grid that has
+// not started yet; the 16-byte response lands in shared memory at `resp`
+// (16-byte aligned) and completes 16 transaction bytes on `bar`.  After one
+// failed response a CTA must not ask again.
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint32_t bar)
+{
+    asm volatile(
+        "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];" ::"r"(
+            resp),
+        "r"(bar)
+        : "memory");
+}
+
+// Read a response: true and the x index of the first CTA of the cancelled
+// cluster, or false when no cluster was left to cancel.
+__device__ __forceinline__ bool clc_query(uint32_t resp, int& first_ctaid_x)
+{
+    uint32_t ok, x = 0;
+    asm volatile(
+        "{\n\t.reg .b128 r;\n\t.reg .pred p;\n\t"
+        "ld.shared.b128 r, [%2];\n\t"
+        "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t"
+        "@p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, r;\n\t}"
+        : "=r"(ok), "+r"(x)
+        : "r"(resp)
+        : "memory");
+    first_ctaid_x = static_cast<int>(x);
+    return ok != 0;
+}
+
 // ------------------------------------------------------------------- TMA --
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map)
@@ -241,6 +289,13 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank)
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr)
 {
     asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Arrive with cluster-scope release: publishes this thread's earlier writes
+// into another CTA's shared memory (st_cluster_u32) to that CTA's waiters.
+__device__ __forceinline__ void mbar_arrive_cluster_release(uint32_t cluster_addr)
+{
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 __device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v)

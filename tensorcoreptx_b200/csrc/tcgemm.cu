@@ -103,9 +103,11 @@ tcg_status encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
     return TCG_SUCCESS;
 }
 
-// Tile shape.  Candidates: CTA-pair 256 x BN tiles (BN 256/128, one pair per
-// two SMs) and single-CTA 128 x BN tiles (BN 256/128/64, one per SM).
-// Cost = waves of persistent units x BN / efficiency, the critical path in
+// Tile shape.  Problems that fill a wave of SM pairs with 512 x 256 tiles
+// use that pair-wide tile.  Below that the candidates are CTA-pair 256 x BN
+// tiles (BN 256/128, one pair per two SMs) and single-CTA 128 x BN tiles
+// (BN 256/128/64, one per SM), with
+// cost = waves of persistent units x BN / efficiency, the critical path in
 // units of one SM's 128-column share of a tile, where efficiency is the
 // measured per-SM throughput of the shape relative to the 256 x 256 pair
 // (int8 on B200, 4096..16384 cubed: the pair reads a third less operand data
@@ -120,7 +122,9 @@ struct TileChoice {
 // TCG_TILE_N = 64|128|256, TCG_CTA_PAIR = 1 (single) | 2 (pair),
 // TCG_GROUP_M = band height in tiles, TCG_K_ALT = 0|1, TCG_UNITS = at most
 // this many persistent CTAs (pairs of CTAs for pair tiles), TCG_TMA_STORE = 0
-// (write C with plain stores instead of TMA stores).
+// (write C with plain stores instead of TMA stores), TCG_TAIL_SPLIT = 0 (no
+// half tiles in the last wave), TCG_STATIC_SCHEDULE = 1 (persistent units
+// with round-robin work items instead of cluster launch control).
 int env_int(const char* name, int dflt = 0)
 {
     const char* v = std::getenv(name);
@@ -132,7 +136,7 @@ TileChoice choose_tile(int M, int N, int K, int elem_bytes, int batches, int sms
     static const int env_bn = env_int("TCG_TILE_N");
     static const int env_pair = env_int("TCG_CTA_PAIR");
     const int forced_bn = g_force_bn.load() ? g_force_bn.load() : env_bn;
-    // 0 auto, 1 single, 2 pair, 3 wide
+    // 0 auto, 1 single, 2 pair, 3 wide, 4 pair-wide
     const int forced = g_force_pair.load() ? g_force_pair.load() : env_pair;
     struct Cand {
         int shape;
@@ -141,24 +145,22 @@ TileChoice choose_tile(int M, int N, int K, int elem_bytes, int batches, int sms
     };
     static const Cand cands[] = {{kShapePair, 256, 1.00}, {kShapeSingle, 256, 0.87}, {kShapePair, 128, 0.72},
                                  {kShapeSingle, 128, 0.72}, {kShapeSingle, 64, 0.50}};
-    // Measured on B200: once the operand panels one wave of pair tiles streams
-    // (about 4400 rows x K bytes at 256 x 256) no longer fit in L2, pair
-    // tiles pull about twice the DRAM bytes of single-CTA tiles and lose to
-    // them (int8 32768^3: 59 GB vs 29 GB per launch, 2.2 vs 2.5 POPS
-    // sustained).  Such problems use the wide single-CTA 256 x 256 tile
-    // (24.7 GB, 2.75 POPS sustained there), which trades the accumulator
-    // double buffer -- cheap when K is this long -- for pair-like operand
-    // reuse without the cross-SM coupling.
-    const double wave_bytes = 4400.0 * static_cast<double>(K) * elem_bytes;
-    const long long pair_tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256) * batches;
-    const bool pair_thrashes = wave_bytes > 100e6 && pair_tiles >= 4LL * (sms / 2);
-    if (forced == 3 || (!forced && !forced_bn && pair_thrashes)) return TileChoice{256, kShapeWide};
+    // Measured on B200 (int8 and fp16, 4096..32768 cubed, work items handed
+    // out in order by cluster launch control): the pair 512 x 256 tile --
+    // the least operand traffic from L2 per MAC (48 bytes per clock per SM at
+    // the int8 rate, against 64 for 256 x 256 tiles) -- is the fastest shape
+    // once it fills a wave of SM pairs (int8 8192^3: 3202 TOPS against 3029
+    // for pair 256 x 256 and 3071 for wide; fp16 8192^3: 1512 against 1393
+    // and 1473 TFLOP/s); at int8 4096^3 its 1.73 waves cost what the traffic
+    // saves (all shapes within 1 %).  Smaller problems are sized by waves.
+    const long long pw_tiles = static_cast<long long>((M + 511) / 512) * ((N + 255) / 256) * batches;
+    if (forced == 4 || (!forced && !forced_bn && pw_tiles >= sms / 2)) return TileChoice{256, kShapePairWide};
+    if (forced == 3) return TileChoice{256, kShapeWide};
     TileChoice best{256, kShapePair};
     double best_cost = -1.0;
     for (const Cand& c : cands) {
         const bool pair = c.shape == kShapePair;
         if ((forced == 1 && pair) || (forced == 2 && !pair)) continue;
-        if (!forced && pair && pair_thrashes) continue;
         if (forced_bn && c.bn != forced_bn) continue;
         if (i8_mn && (pair ? c.bn / 2 : c.bn) < 128) continue;  // whole 128-byte atoms
         const long long tm = (M + (pair ? 255 : 127)) / (pair ? 256 : 128);
@@ -207,8 +209,8 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
 {
     void* const* extra = epi.extra;
     const int n_extra = epi.n_extra;
-    constexpr bool kPair = kShape == kShapePair;
-    constexpr int kStages = kShape == kShapeWide ? 3
+    constexpr bool kPair = kShape == kShapePair || kShape == kShapePairWide;
+    constexpr int kStages = kShape == kShapeWide ? 3 : kShape == kShapePairWide ? 4
                             : kPair ? (kBN == 256 ? 6 : 8) : (kBN == 256 ? 4 : (kBN == 128 ? 6 : 8));
     constexpr bool kByte = kKind != kKindF16;
     using T = GemmTraits<kKind, kAccF16, kBMn, kBN, kStages, kShape>;
@@ -228,13 +230,18 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
 
     const CUtensorMapDataType dt = kByte ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const uint64_t es = T::kElem;
-    CUtensorMap mA, mB;
+    CUtensorMap mA, mB, mBh;  // mBh: B boxes of half the rows, for half tiles (K-major B)
     tcg_status s = encode_3d(&mA, dt, A, K, M, batches, K * es, static_cast<uint64_t>(M) * K * es, T::kBK, kBM);
     if (s != TCG_SUCCESS) return s;
-    if (kBMn)  // B is K x N, N contiguous
+    if (kBMn) {  // B is K x N, N contiguous; half tiles load fewer 128-byte atoms
         s = encode_3d(&mB, dt, B, N, K, batches, N * es, static_cast<uint64_t>(K) * N * es, T::kAtomN, T::kBK);
-    else  // B is N x K, K contiguous
+        mBh = mB;
+    } else {  // B is N x K, K contiguous
         s = encode_3d(&mB, dt, B, K, N, batches, K * es, static_cast<uint64_t>(N) * K * es, T::kBK, T::kBRows);
+        if (s == TCG_SUCCESS)
+            s = encode_3d(&mBh, dt, B, K, N, batches, K * es, static_cast<uint64_t>(N) * K * es, T::kBK,
+                          T::kBRows / 2);
+    }
     if (s != TCG_SUCCESS) return s;
 
     GemmParams p;
@@ -257,12 +264,17 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     p.l2_a = env_l2a;
     p.l2_b = env_l2b;
     p.n_extra = n_extra;
-    if constexpr (kKind == kKindI8)
-        p.idesc = make_idesc(2u, 1u, 1u, kBMn, T::kUmmaM, kBN);  // S32 <- s8 x s8
-    else if constexpr (kKind == kKindF8)
-        p.idesc = make_idesc(1u, epi.a_fmt, epi.b_fmt, kBMn, T::kUmmaM, kBN);  // F32 <- e4m3/e5m2
-    else
-        p.idesc = make_idesc(kAccF16 ? 0u : 1u, 0u, 0u, kBMn, T::kUmmaM, kBN);  // F32|F16 <- f16
+    // instruction descriptors of a whole tile (N = kBN) and of a half tile
+    const auto idesc_for = [&](int n) {
+        if constexpr (kKind == kKindI8)
+            return make_idesc(2u, 1u, 1u, kBMn, T::kUmmaM, n);  // S32 <- s8 x s8
+        else if constexpr (kKind == kKindF8)
+            return make_idesc(1u, epi.a_fmt, epi.b_fmt, kBMn, T::kUmmaM, n);  // F32 <- e4m3/e5m2
+        else
+            return make_idesc(kAccF16 ? 0u : 1u, 0u, 0u, kBMn, T::kUmmaM, n);  // F32|F16 <- f16
+    };
+    p.idesc = idesc_for(kBN);
+    p.idesc_half = idesc_for(kBN / 2);
     p.scale_a = epi.scale_a;
     p.scale_b = epi.scale_b;
     for (int i = 0; i < kMaxExtraDst; ++i) p.extra[i] = i < n_extra ? extra[i] : nullptr;
@@ -283,17 +295,19 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     p.timeout_ns = g_timeout_ns.load();
 
     const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n * batches;
-    if (tiles > 0x7fffffffLL) return TCG_ERR_SHAPE;
+    if (tiles > 0x3fffffffLL) return TCG_ERR_SHAPE;
     static const int env_units = env_int("TCG_UNITS");  // cap on persistent CTAs (pairs), tuning only
+    static const int env_split = env_int("TCG_TAIL_SPLIT", 1);
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof cfg);
+    cudaLaunchAttribute attr[1];
+    long long units = dev.sms;
     if constexpr (kPair) {
         const long long pairs = dev.sms / 2;
-        cudaLaunchConfig_t cfg;
-        std::memset(&cfg, 0, sizeof cfg);
-        cfg.gridDim = dim3(static_cast<unsigned>(2 * (tiles < pairs ? tiles : pairs)), 1, 1);
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
         cfg.blockDim = dim3(kThreads, 1, 1);
         cfg.dynamicSmemBytes = T::kSmemBytes;
         cfg.stream = st;
-        cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = 2;
         attr[0].val.clusterDim.y = 1;
@@ -310,19 +324,42 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
             }
             max_clusters[dev_id] = n;
         }
-        long long units = max_clusters[dev_id] < pairs ? max_clusters[dev_id] : pairs;
-        if (env_units > 0 && env_units < units) units = env_units;
-        cfg.gridDim = dim3(static_cast<unsigned>(2 * (tiles < units ? tiles : units)), 1, 1);
-        static const int debug = env_int("TCG_DEBUG");
-        if (debug)
-            std::fprintf(stderr, "tcgemm: pair grid %u (max clusters %d) tile 256x%d stages %d group_m %d kalt %d\n",
-                         cfg.gridDim.x, max_clusters[dev_id], kBN, kStages, p.group_m, p.k_alternate);
-        e = cudaLaunchKernelEx(&cfg, kern, mA, mB, mC, p);
+        units = max_clusters[dev_id] < pairs ? max_clusters[dev_id] : pairs;
+    }
+    if (env_units > 0 && env_units < units) units = env_units;
+    // Tail split: when the last wave of tiles would leave at least half of the
+    // units idle, its tiles are cut into column halves (two work items each),
+    // which the idle units take; that wave then lasts about half as long.
+    // Each half is an ordinary tile of N = kBN / 2: no cross-unit reduction,
+    // and every output element is computed exactly as without the split.
+    constexpr bool kCanSplit = !kBMn || (T::kBRows / 2) % T::kAtomN == 0;
+    const long long rem = tiles % units;
+    p.split_from = static_cast<int>(tiles);
+    if (kCanSplit && env_split && rem > 0 && 2 * rem <= units) p.split_from = static_cast<int>(tiles - rem);
+    const long long work = p.split_from + 2 * (tiles - p.split_from);
+    // Scheduling.  Dynamic (the default whenever there is more than one wave
+    // of work): one cluster (CTA) per work item; the clusters the GPU can hold
+    // start, and each, when it finishes an item, takes over the next
+    // not-yet-started cluster's item through cluster launch control -- in
+    // launch order, so the items in flight stay a contiguous stretch of the
+    // rasterised order however unevenly the units progress, and L2 keeps
+    // serving the operand panels they share.  Static: one persistent unit per
+    // resident slot, items round-robin.
+    static const int env_static = env_int("TCG_STATIC_SCHEDULE");
+    p.dynamic = (!env_static && work > units && (kPair ? 2 : 1) * work <= 0x7fffffffLL) ? 1 : 0;
+    p.wave_units = static_cast<int>(units);
+    const long long grid_units = p.dynamic ? work : (work < units ? work : units);
+    static const int debug = env_int("TCG_DEBUG");
+    if (debug)
+        std::fprintf(stderr, "tcgemm: %s tile %dx%d stages %d units %lld grid %lld tiles %lld split_from %d group_m %d kalt %d %s\n",
+                     kPair ? "pair" : (T::kWide ? "wide" : "single"), T::kTileM, kBN, kStages, units,
+                     grid_units, tiles, p.split_from, p.group_m, p.k_alternate, p.dynamic ? "dynamic" : "static");
+    if constexpr (kPair) {
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * grid_units), 1, 1);
+        e = cudaLaunchKernelEx(&cfg, kern, mA, mB, mBh, mC, p);
         if (e != cudaSuccess) return cuda_fail(e);
     } else {
-        int grid = static_cast<int>(tiles < dev.sms ? tiles : dev.sms);
-        if (env_units > 0 && env_units < grid) grid = env_units;
-        kern<<<grid, kThreads, T::kSmemBytes, st>>>(mA, mB, mC, p);
+        kern<<<static_cast<int>(grid_units), kThreads, T::kSmemBytes, st>>>(mA, mB, mBh, mC, p);
     }
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
@@ -338,6 +375,8 @@ tcg_status dispatch_bn(DeviceState& dev, const void* A, const void* B, void* C, 
     constexpr bool kByteMn = kKind != kKindF16 && kBMn;  // MN-major byte operand: 128-column atoms
     const TileChoice c = choose_tile(M, N, K, kKind == kKindF16 ? 2 : 1, batches, dev.sms, kByteMn);
     if (c.shape == kShapeWide) return launch_gemm<kKind, kAccF16, kBMn, 256, kShapeWide>(dev, A, B, C, M, N, K, batches, st, epi);
+    if (c.shape == kShapePairWide)
+        return launch_gemm<kKind, kAccF16, kBMn, 256, kShapePairWide>(dev, A, B, C, M, N, K, batches, st, epi);
     if (c.shape == kShapePair) {
         if (c.bn == 128) {
             // an MN-major byte pair tile needs 128 columns per CTA

@@ -171,7 +171,8 @@ def set_tile_n(bn: int) -> None:
 
 def set_cta_pair(mode: int) -> None:
     """Force the CTA shape: 0 automatic, 1 single-CTA 128-row tiles, 2 two-CTA
-    (cta_group::2) 256-row tiles."""
+    (cta_group::2) 256-row tiles, 3 single-CTA 256 x 256 tiles, 4 two-CTA
+    512 x 256 tiles."""
     nat.lib().tcg_set_cta_pair(int(mode))
 
 

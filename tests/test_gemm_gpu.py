@@ -400,8 +400,9 @@ _SHAPE_CASES = [(1, 300, 528, 384), (2, 260, 144, 128), (1, 512, 1024, 256)]
 @pytest.mark.parametrize("prec", ["int8", "int8_kn", "int4", "fp16", "fp16_nk", "fp16acc"])
 def test_every_tile_shape_gives_identical_results(prec):
     """Single-CTA 128-row tiles (widths 64/128/256), CTA-pair 256-row tiles
-    (widths 128/256) and single-CTA 256 x 256 tiles with two accumulators must
-    all produce the same C: integer results equal the
+    (widths 128/256), single-CTA 256 x 256 tiles with two accumulators and
+    CTA-pair 512 x 256 tiles must all produce the same C: integer results
+    equal the
     oracle, and fp16 results are bit-identical across shapes because every
     element accumulates in the same k order."""
     T = tcg()
@@ -426,14 +427,14 @@ def test_every_tile_shape_gives_identical_results(prec):
                 (lambda: T.gemm_fp16(_cuda(A, torch.float16), _cuda(B, torch.float16), acc=acc))
         outs = {}
         try:
-            for mode, bns in ((1, (64, 128, 256)), (2, (128, 256)), (3, (256,))):
+            for mode, bns in ((1, (64, 128, 256)), (2, (128, 256)), (3, (256,)), (4, (256,))):
                 for bn in bns:
                     T.set_cta_pair(mode)
                     T.set_tile_n(bn)
                     outs[(mode, bn)] = fn().cpu().numpy()
                     shape_used = (T.last_tile_m(), T.last_tile_n())
                     if not (prec == "int8_kn" and (mode, bn) in ((1, 64), (2, 128))):
-                        assert shape_used == ((128, 256, 256)[mode - 1], bn), (prec, mode, bn, shape_used)
+                        assert shape_used == ((128, 256, 256, 512)[mode - 1], bn), (prec, mode, bn, shape_used)
         finally:
             T.set_cta_pair(0)
             T.set_tile_n(0)
@@ -454,6 +455,42 @@ def test_every_tile_shape_gives_identical_results(prec):
             else:
                 ref = O.gemm_f16_f64(Ab, Bb, b_kn=(prec != "fp16_nk"), threads=8)
                 assert np.abs(out_b - ref).max() <= f16_tol(Ab, Bb, K)
+
+
+@pytest.mark.parametrize("prec", ["int8", "fp16"])
+def test_tail_split_multiwave(prec):
+    """3328^2 outputs make more tiles than one wave for every tile shape
+    (169 pair or wide 256 x 256 tiles over 74 pairs / 148 CTAs, 338 single
+    128 x 256 tiles over 148 CTAs, 91 pair 512 x 256 tiles over 74 pairs)
+    with a last wave under half full, so the last tiles run as column halves.  Results must still equal the oracle
+    (int8) and be bit-identical across shapes (fp16: same k order)."""
+    T = tcg()
+    rng = np.random.default_rng(77)
+    M = N = 3328
+    K = 256 if prec == "int8" else 128
+    if prec == "int8":
+        A, B = rand_s8(rng, (M, K)), rand_s8(rng, (N, K))
+        fn = lambda: T.gemm_int8(_cuda(A), _cuda(B))
+    else:
+        A, B = rand_f16_bits(rng, (M, K)), rand_f16_bits(rng, (K, N))
+        fn = lambda: T.gemm_fp16(_cuda(A, torch.float16), _cuda(B, torch.float16))
+    outs = {}
+    try:
+        for mode in (1, 2, 3, 4):
+            T.set_cta_pair(mode)
+            T.set_tile_n(256)
+            outs[mode] = fn().cpu().numpy()
+    finally:
+        T.set_cta_pair(0)
+        T.set_tile_n(0)
+    for mode, out in outs.items():
+        assert np.array_equal(out.view(np.uint32), outs[2].view(np.uint32)), mode
+    if prec == "int8":
+        assert np.array_equal(outs[2], O.gemm_s8(A, B, threads=8))
+    else:
+        rows = np.r_[0:64, M - 300:M]  # includes the last tiles, which run as halves
+        ref = O.gemm_f16_f64(A[rows], B, b_kn=True, threads=8)
+        assert np.abs(outs[2][rows] - ref).max() <= f16_tol(A, B, K)
 
 
 # ------------------------------------------------------- host-buffer entry --
