@@ -4,22 +4,25 @@
 // kernels/int8_*.cu and, after widening to int8, kernels/int4_*.cu) with one
 // Blackwell-native design:
 //
-//   * persistent CTAs (grid <= #SMs), static round-robin over output tiles,
-//     grouped rasterisation (bands of tile-rows) for L2 reuse;
+//   * tile shapes from 128 x 64 (one CTA) to 512 x 256 (a CTA pair issuing
+//     tcgen05.mma.cta_group::2), grouped rasterisation (bands of tile-rows);
+//   * scheduling: one cluster per work item, running clusters taking over
+//     not-yet-started ones in launch order with cluster launch control (or,
+//     for a single wave, persistent units round-robin);
 //   * warp specialisation, 192 threads:
 //       warp 0 lane 0  -- TMA producer: 128-byte-swizzled A and B tiles into a
-//                         kStages-deep shared-memory ring (full/empty mbarriers);
+//                         kStages-deep shared-memory ring (full/empty
+//                         mbarriers); in the leader CTA also the scheduler;
 //       warp 1         -- allocates tensor memory; lane 0 issues tcgen05.mma
-//                         (kind::f16 or kind::i8, M=128, N=kBN) into a
-//                         double-buffered TMEM accumulator and releases ring
-//                         slots with tcgen05.commit;
-//       warps 2..5     -- epilogue: tcgen05.ld TMEM -> registers -> global C,
-//                         overlapping the mainloop of the next tile;
+//                         into TMEM accumulators and releases ring slots with
+//                         tcgen05.commit;
+//       warps 2..5     -- epilogue, one per TMEM lane quarter: tcgen05.ld
+//                         TMEM -> registers -> TMA store of C;
 //   * every mbarrier wait is bounded: on expiry the kernel records a failure
 //     word, drains its own copies in flight, frees TMEM and returns.
 //
-// One CTA computes a 128 x kBN tile of C; one ring stage holds 128 bytes of K
-// (64 fp16 or 128 int8 values) for A (128 rows) and B (kBN rows/cols).
+// One ring stage holds 128 bytes of K (64 fp16 or 128 int8 values) for the
+// CTA's rows of A and of B.
 #pragma once
 
 #include <cuda_fp16.h>
