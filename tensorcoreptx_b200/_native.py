@@ -73,6 +73,8 @@ class TcgError(RuntimeError):
 def lib():
     """Load libtcgemm.so once; raise ImportError if it is not built."""
     global _lib
+    if _lib is not None:
+        return _lib
     with _lock:
         if _lib is None:
             if not os.path.exists(LIB_PATH):

@@ -817,25 +817,49 @@ __device__ __forceinline__ void widen_word(uint32_t w, uint32_t& o0, uint32_t& o
     o1 = __byte_perm(lo, hi, 0x7362);  // lo2 hi2 lo3 hi3
 }
 
-__global__ void unpack_s4_kernel(const uint4* __restrict__ in, uint4* __restrict__ out, long long n16,
-                                 const int8_t* __restrict__ tail_in, int8_t* __restrict__ tail_out,
-                                 int tail)
+// Two tensors (A and B of an int4 GEMM) in one launch: 16-byte chunks
+// [0, n0) of segment 0 then [0, n1) of segment 1, two chunks per thread per
+// step; each segment's last n % 16 bytes (tail0, tail1) by block 0.
+struct UnpackSeg {
+    const uint4* in;
+    uint4* out;
+    long long n16;
+    const int8_t* tail_in;
+    int8_t* tail_out;
+    int tail;
+};
+
+__device__ __forceinline__ void unpack_chunk(const UnpackSeg& s, long long i)
 {
+    const uint4 v = s.in[i];
+    uint4 a, b;
+    widen_word(v.x, a.x, a.y);
+    widen_word(v.y, a.z, a.w);
+    widen_word(v.z, b.x, b.y);
+    widen_word(v.w, b.z, b.w);
+    s.out[2 * i] = a;
+    s.out[2 * i + 1] = b;
+}
+
+__global__ void unpack_s4_kernel(const UnpackSeg s0, const UnpackSeg s1)
+{
+    const long long total = s0.n16 + s1.n16;
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16; i += stride) {
-        const uint4 v = in[i];
-        uint4 a, b;
-        widen_word(v.x, a.x, a.y);
-        widen_word(v.y, a.z, a.w);
-        widen_word(v.z, b.x, b.y);
-        widen_word(v.w, b.z, b.w);
-        out[2 * i] = a;
-        out[2 * i + 1] = b;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += 2 * stride) {
+        const long long j = i + stride;
+        if (i < s0.n16) unpack_chunk(s0, i); else unpack_chunk(s1, i - s0.n16);
+        if (j < total) {
+            if (j < s0.n16) unpack_chunk(s0, j); else unpack_chunk(s1, j - s0.n16);
+        }
     }
-    if (blockIdx.x == 0 && threadIdx.x < tail) {
-        const int8_t x = tail_in[threadIdx.x];
-        tail_out[2 * threadIdx.x] = static_cast<int8_t>(static_cast<int8_t>(x << 4) >> 4);
-        tail_out[2 * threadIdx.x + 1] = static_cast<int8_t>(x >> 4);
+    if (blockIdx.x == 0) {
+        const UnpackSeg& s = threadIdx.x < 16 ? s0 : s1;
+        const int k = threadIdx.x & 15;
+        if (threadIdx.x < 32 && k < s.tail) {
+            const int8_t x = s.tail_in[k];
+            s.tail_out[2 * k] = static_cast<int8_t>(static_cast<int8_t>(x << 4) >> 4);
+            s.tail_out[2 * k + 1] = static_cast<int8_t>(x >> 4);
+        }
     }
 }
 

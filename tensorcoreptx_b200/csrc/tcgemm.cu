@@ -85,9 +85,57 @@ tcg_status resolve_encode()
     return g_encode ? TCG_SUCCESS : TCG_ERR_CUDA;
 }
 
+// Recently encoded tensor maps, per host thread (no locking): a map depends
+// only on its arguments, so calls that repeat a buffer and shape -- the
+// common case for GEMMs in a loop -- skip the driver's encoder.
+struct MapKey {
+    const void* base;
+    uint64_t d0, d1, d2, s1, s2;
+    uint32_t box0, box1;
+    int dt;
+    bool operator==(const MapKey& o) const
+    {
+        return base == o.base && d0 == o.d0 && d1 == o.d1 && d2 == o.d2 && s1 == o.s1 && s2 == o.s2 &&
+               box0 == o.box0 && box1 == o.box1 && dt == o.dt;
+    }
+};
+struct MapCache {
+    static constexpr int kEntries = 16;
+    MapKey key[kEntries];
+    CUtensorMap map[kEntries];
+    bool used[kEntries] = {};
+    int next = 0;
+};
+thread_local MapCache t_map_cache;
+
+tcg_status encode_3d_uncached(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
+                              uint64_t d2, uint64_t s1, uint64_t s2, uint32_t box0, uint32_t box1);
+
 // 3-D tiled map: dims {d0 (contiguous), d1, d2}, byte strides of d1 and d2.
 tcg_status encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
                      uint64_t d2, uint64_t s1, uint64_t s2, uint32_t box0, uint32_t box1)
+{
+    const MapKey k{base, d0, d1, d2, s1, s2, box0, box1, static_cast<int>(dt)};
+    MapCache& c = t_map_cache;
+    for (int i = 0; i < MapCache::kEntries; ++i) {
+        if (c.used[i] && c.key[i] == k) {
+            *map = c.map[i];
+            return TCG_SUCCESS;
+        }
+    }
+    const tcg_status s = encode_3d_uncached(map, dt, base, d0, d1, d2, s1, s2, box0, box1);
+    if (s == TCG_SUCCESS) {
+        const int i = c.next;
+        c.next = (c.next + 1) % MapCache::kEntries;
+        c.key[i] = k;
+        c.map[i] = *map;
+        c.used[i] = true;
+    }
+    return s;
+}
+
+tcg_status encode_3d_uncached(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
+                              uint64_t d2, uint64_t s1, uint64_t s2, uint32_t box0, uint32_t box1)
 {
     cuuint64_t dims[3] = {d0, d1, d2};
     cuuint64_t strides[2] = {s1, s2};
@@ -422,17 +470,30 @@ tcg_status prologue(const void* A, const void* B, void* C, int M, int N, int K, 
 
 size_t round256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-tcg_status launch_unpack(const int8_t* in, int8_t* out, size_t n_packed, int sms, cudaStream_t st)
+UnpackSeg unpack_seg(const int8_t* in, int8_t* out, size_t n_packed)
 {
-    const long long n16 = static_cast<long long>(n_packed / 16);
-    const int tail = static_cast<int>(n_packed % 16);
-    long long blocks = (n16 + 255) / 256;
+    UnpackSeg g;
+    g.n16 = static_cast<long long>(n_packed / 16);
+    g.in = reinterpret_cast<const uint4*>(in);
+    g.out = reinterpret_cast<uint4*>(out);
+    g.tail_in = in + g.n16 * 16;
+    g.tail_out = out + g.n16 * 32;
+    g.tail = static_cast<int>(n_packed % 16);
+    return g;
+}
+
+// Widen one or two packed int4 tensors (n1 = 0: one) in a single launch.
+tcg_status launch_unpack(const int8_t* in0, int8_t* out0, size_t n0, const int8_t* in1, int8_t* out1, size_t n1,
+                         int sms, cudaStream_t st)
+{
+    const UnpackSeg s0 = unpack_seg(in0, out0, n0);
+    const UnpackSeg s1 = n1 ? unpack_seg(in1, out1, n1) : unpack_seg(in0, out0, 0);
+    const long long chunks = s0.n16 + s1.n16;
+    long long blocks = (chunks + 511) / 512;  // two chunks per thread
     const long long cap = static_cast<long long>(sms) * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    unpack_s4_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(
-        reinterpret_cast<const uint4*>(in), reinterpret_cast<uint4*>(out), n16, in + n16 * 16, out + n16 * 32,
-        tail);
+    unpack_s4_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(s0, s1);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TCG_SUCCESS : cuda_fail(e);
 }
@@ -582,9 +643,8 @@ tcg_status gemm_s4_impl(const int8_t* A_packed, const int8_t* BT_packed, void* C
     }
     int8_t* a8 = static_cast<int8_t*>(ws);
     int8_t* b8 = a8 + round256(static_cast<size_t>(batches) * M * K);
-    s = launch_unpack(A_packed, a8, static_cast<size_t>(batches) * M * (K / 2), dev->sms, st);
-    if (s == TCG_SUCCESS)
-        s = launch_unpack(BT_packed, b8, static_cast<size_t>(batches) * N * (K / 2), dev->sms, st);
+    s = launch_unpack(A_packed, a8, static_cast<size_t>(batches) * M * (K / 2), BT_packed, b8,
+                      static_cast<size_t>(batches) * N * (K / 2), dev->sms, st);
     if (s == TCG_SUCCESS) s = dispatch_bn<kKindI8, false, false>(*dev, a8, b8, C, M, N, K, batches, st, epi);
     if (owned) {
         cudaError_t e = cudaFreeAsync(ws, st);
@@ -739,7 +799,7 @@ tcg_status tcg_unpack_s4(const int8_t* packed, int8_t* out, size_t n_packed, voi
     DeviceState* dev;
     tcg_status s = device_state(&dev);
     if (s != TCG_SUCCESS) return s;
-    return launch_unpack(packed, out, n_packed, dev->sms, static_cast<cudaStream_t>(stream));
+    return launch_unpack(packed, out, n_packed, nullptr, nullptr, 0, dev->sms, static_cast<cudaStream_t>(stream));
 }
 
 tcg_status tcg_check_device_error(void* stream, uint64_t* word)

@@ -19,7 +19,13 @@ import torch
 from . import _native as nat
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream_ptr(t: torch.Tensor) -> int:
+    """The current CUDA stream of t's device, as a raw handle."""
+    if _raw_stream is not None:
+        return _raw_stream(t.get_device())
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
