@@ -481,6 +481,11 @@ def extras():
         out["int8_4096_torch_int_mm"] = {"tops": 2 * n ** 3 / ms_lib / 1e9, "ms": ms_lib}
     except Exception as e:  # pragma: no cover
         out["int8_4096_torch_int_mm"] = {"error": str(e)[:80]}
+    # the same with B row-major (K x N), the layout the configuration names
+    B_kn = BT.t().contiguous()
+    ms = time_fn(lambda: T.gemm_int8_kn(A, B_kn), 50)
+    out["int8_4096_b_row_major"] = {"tops": 2 * n ** 3 / ms / 1e9, "ms": ms}
+    del B_kn
     Ap = torch.randint(-128, 128, (n, n // 2), generator=g, device=dev, dtype=torch.int8)
     Bp = torch.randint(-128, 128, (n, n // 2), generator=g, device=dev, dtype=torch.int8)
     ws = torch.empty(T.int4_workspace_size(n, n, n), dtype=torch.uint8, device=dev)
