@@ -17,9 +17,10 @@ KERNELS = {
     "fp16_wmma": "fp16", "fp16_ptx_fp16acc": "fp16",
     "int8_wmma": "int8", "int8_ptx_mma_k32": "int8",
     "int4_wmma": "int4", "int4_ptx_mma_k64_x4_x2nontrans_ca": "int4",
+    "int4_ptx_mma_k64_x2_x2nontrans_ca": "int4",
 }
 K_TILE = {"fp16_wmma": 16, "fp16_ptx_fp16acc": 16, "int8_wmma": 16, "int8_ptx_mma_k32": 32,
-          "int4_wmma": 32, "int4_ptx_mma_k64_x4_x2nontrans_ca": 64}
+          "int4_wmma": 32, "int4_ptx_mma_k64_x4_x2nontrans_ca": 64, "int4_ptx_mma_k64_x2_x2nontrans_ca": 64}
 
 _libs = {}
 

@@ -66,6 +66,23 @@ def test_reference_int4_kernel_verify_512(name):
     assert acc.pass_ and C[0, 0] == -563
 
 
+def test_negative_control_reference_kernel_is_flagged():
+    """The reference's known-wrong int4 kernel (x2_x2 ldmatrix mapping), run
+    on the verify inputs: the checker must fail it exactly as the
+    reference's own log did (max_abs 2363 at (304,455), ref 1182, out -1181)."""
+    name = "int4_ptx_mma_k64_x2_x2nontrans_ca"
+    _need(name)
+    nc = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "known_answers.json")))[
+        "int4_negative_control"]
+    A, BT = O.generate_int4_packed(512, 512, 512)
+    C = RK.run(name, torch.from_numpy(A[0]).to(DEV), torch.from_numpy(BT[0]).to(DEV),
+               512, 512, 512).cpu().numpy()
+    acc = O.measure_accuracy_i32(O.gemm_s4(A[0], BT[0], 512, threads=8), C)
+    assert not acc.pass_
+    assert (acc.max_abs_err, acc.max_row, acc.max_col, acc.ref_at_max, acc.out_at_max) == \
+        (nc["max_abs"], nc["row"], nc["col"], nc["ref"], nc["bad_out"])
+
+
 @pytest.mark.parametrize("name", ["fp16_wmma", "fp16_ptx_fp16acc"])
 def test_reference_fp16_kernel_within_same_tolerance(name):
     """The tolerance our fp16 path meets, applied to the reference's output."""
