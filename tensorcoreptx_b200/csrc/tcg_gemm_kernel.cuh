@@ -337,6 +337,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (kPair) cluster_sync_all();  // the peer's barriers exist before any remote arrival
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Everything above overlaps the previous kernel's tail; global memory is
+    // touched only below.
+    grid_dependency_wait();
+    grid_launch_dependents();
 
     const int num_tiles = p.tiles_m * p.tiles_n * p.batches;
     const int num_work = p.split_from + 2 * (num_tiles - p.split_from);
@@ -843,6 +847,8 @@ __device__ __forceinline__ void unpack_chunk(const UnpackSeg& s, long long i)
 
 __global__ void unpack_s4_kernel(const UnpackSeg s0, const UnpackSeg s1)
 {
+    grid_dependency_wait();
+    grid_launch_dependents();
     const long long total = s0.n16 + s1.n16;
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += 2 * stride) {

@@ -79,6 +79,20 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
     return ok != 0;
 }
 
+// ------------------------------------------- programmatic dependent launch --
+
+// Wait until the grids this launch depends on (the previous kernel on the
+// stream, when launched with programmatic stream serialisation) have
+// completed and their memory is visible; a no-op otherwise.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Let the next kernel on the stream start launching (it still waits for
+// this grid's completion before it touches memory).
+__device__ __forceinline__ void grid_launch_dependents()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------- cluster launch control --
 
 // Ask the hardware to cancel the launch of a cluster of this grid that has

@@ -172,11 +172,18 @@ struct TileChoice {
 // this many persistent CTAs (pairs of CTAs for pair tiles), TCG_TMA_STORE = 0
 // (write C with plain stores instead of TMA stores), TCG_TAIL_SPLIT = 0 (no
 // half tiles in the last wave), TCG_STATIC_SCHEDULE = 1 (persistent units
-// with round-robin work items instead of cluster launch control).
+// with round-robin work items instead of cluster launch control), TCG_PDL = 0
+// (no programmatic dependent launch).
 int env_int(const char* name, int dflt = 0)
 {
     const char* v = std::getenv(name);
     return v ? std::atoi(v) : dflt;
+}
+
+bool pdl_enabled()
+{
+    static const int env_pdl = env_int("TCG_PDL", 1);
+    return env_pdl != 0;
 }
 
 TileChoice choose_tile(int M, int N, int K, int elem_bytes, int batches, int sms, bool i8_mn)
@@ -348,19 +355,20 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     static const int env_split = env_int("TCG_TAIL_SPLIT", 1);
     cudaLaunchConfig_t cfg;
     std::memset(&cfg, 0, sizeof cfg);
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
+    std::memset(attr, 0, sizeof attr);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = T::kSmemBytes;
+    cfg.stream = st;
+    cfg.attrs = attr;
     long long units = dev.sms;
     if constexpr (kPair) {
         const long long pairs = dev.sms / 2;
         cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
-        cfg.blockDim = dim3(kThreads, 1, 1);
-        cfg.dynamicSmemBytes = T::kSmemBytes;
-        cfg.stream = st;
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = 2;
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
         cfg.numAttrs = 1;
         // persistent grid: no more pairs than can be resident at once
         static int max_clusters[kMaxDevices] = {0};
@@ -402,13 +410,17 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
         std::fprintf(stderr, "tcgemm: %s tile %dx%d stages %d units %lld grid %lld tiles %lld split_from %d group_m %d kalt %d %s\n",
                      kPair ? "pair" : (T::kWide ? "wide" : "single"), T::kTileM, kBN, kStages, units,
                      grid_units, tiles, p.split_from, p.group_m, p.k_alternate, p.dynamic ? "dynamic" : "static");
-    if constexpr (kPair) {
-        cfg.gridDim = dim3(static_cast<unsigned>(2 * grid_units), 1, 1);
-        e = cudaLaunchKernelEx(&cfg, kern, mA, mB, mBh, mC, p);
-        if (e != cudaSuccess) return cuda_fail(e);
-    } else {
-        kern<<<static_cast<int>(grid_units), kThreads, T::kSmemBytes, st>>>(mA, mB, mBh, mC, p);
+    // Programmatic dependent launch: this grid may start while the previous
+    // kernel on the stream finishes; it waits (griddepcontrol.wait) before
+    // touching global memory.
+    if (pdl_enabled()) {
+        attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+        ++cfg.numAttrs;
     }
+    cfg.gridDim = dim3(static_cast<unsigned>((kPair ? 2 : 1) * grid_units), 1, 1);
+    e = cudaLaunchKernelEx(&cfg, kern, mA, mB, mBh, mC, p);
+    if (e != cudaSuccess) return cuda_fail(e);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
     t_last_tile_n = kBN;
@@ -493,8 +505,20 @@ tcg_status launch_unpack(const int8_t* in0, int8_t* out0, size_t n0, const int8_
     const long long cap = static_cast<long long>(sms) * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    unpack_s4_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(s0, s1);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof cfg);
+    cudaLaunchAttribute attr[1];
+    std::memset(attr, 0, sizeof attr);
+    cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    if (pdl_enabled()) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, unpack_s4_kernel, s0, s1);
     return e == cudaSuccess ? TCG_SUCCESS : cuda_fail(e);
 }
 
