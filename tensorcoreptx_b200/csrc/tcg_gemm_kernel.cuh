@@ -740,8 +740,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive(tb);
             }
         }
-        // the staging tiles are read, and C written, before the CTA exits
-        if (lane == 0 && nstore) bulk_wait_group_all();
+        // the staging tiles are read before the CTA exits (and its shared
+        // memory with them); the writes to C complete with the grid
+        if (lane == 0 && nstore) bulk_wait_group_read<0>();
         __syncwarp();
     }
 

@@ -392,9 +392,76 @@ def test_runs_on_current_stream():
     assert np.array_equal(C.cpu().numpy(), ref)
 
 
+def test_concurrent_multiwave_gemms_on_two_streams():
+    """Two multi-wave GEMMs (one cluster per work item, cluster launch
+    control) running at the same time on two streams: each grid takes over
+    only its own not-yet-started clusters, so both results stay exact."""
+    T = tcg()
+    rng = np.random.default_rng(21)
+    A1, B1 = rand_s8(rng, (3072, 256)), rand_s8(rng, (2816, 256))
+    A2, B2 = rand_s8(rng, (2560, 384)), rand_s8(rng, (3328, 384))
+    dA1, dB1, dA2, dB2 = _cuda(A1), _cuda(B1), _cuda(A2), _cuda(B2)
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    torch.cuda.synchronize()
+    outs1, outs2 = [], []
+    for _ in range(3):
+        with torch.cuda.stream(s1):
+            outs1.append(T.gemm_int8(dA1, dB1))
+        with torch.cuda.stream(s2):
+            outs2.append(T.gemm_int8(dA2, dB2))
+    torch.cuda.synchronize()
+    ref1 = O.gemm_s8(A1, B1, threads=8)
+    ref2 = O.gemm_s8(A2, B2, threads=8)
+    for c in outs1:
+        assert np.array_equal(c.cpu().numpy(), ref1)
+    for c in outs2:
+        assert np.array_equal(c.cpu().numpy(), ref2)
+    assert T.check_device_error() == 0
+
+
+def test_cuda_graph_replay_with_new_inputs():
+    """A CUDA graph holding a multi-wave int8 GEMM and the int4 widen -> GEMM
+    chain (programmatic dependent launches, cluster launch control),
+    replayed after new inputs are written into the captured buffers: every
+    replay computes the new product."""
+    T = tcg()
+    rng = np.random.default_rng(22)
+    M, N, K = 3328, 2560, 256
+    dA = torch.empty((M, K), dtype=torch.int8, device=DEV)
+    dB = torch.empty((N, K), dtype=torch.int8, device=DEV)
+    dAp = torch.empty((1024, 256), dtype=torch.int8, device=DEV)
+    dBp = torch.empty((768, 256), dtype=torch.int8, device=DEV)
+    ws = torch.empty(T.int4_workspace_size(1024, 768, 512), dtype=torch.uint8, device=DEV)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):  # warm up: kernel attributes, tensor maps
+            T.gemm_int8(dA, dB)
+            T.gemm_int4(dAp, dBp, ws)
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        C8 = T.gemm_int8(dA, dB)
+        C4 = T.gemm_int4(dAp, dBp, ws)
+    for _ in range(3):
+        A, B = rand_s8(rng, (M, K)), rand_s8(rng, (N, K))
+        Ap, Bp = rand_s4_packed(rng, 1024, 512), rand_s4_packed(rng, 768, 512)
+        dA.copy_(_cuda(A))
+        dB.copy_(_cuda(B))
+        dAp.copy_(_cuda(Ap))
+        dBp.copy_(_cuda(Bp))
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        assert np.array_equal(C8.cpu().numpy(), O.gemm_s8(A, B, threads=8))
+        assert np.array_equal(C4.cpu().numpy(), O.gemm_s4(Ap, Bp, 512, threads=8))
+    del g
+    assert T.check_device_error() == 0
+
+
 # ------------------------------------------------- tile shapes & CTA pairs --
 
-_SHAPE_CASES = [(1, 300, 528, 384), (2, 260, 144, 128), (1, 512, 1024, 256)]
+_SHAPE_CASES =[(1, 300, 528, 384), (2, 260, 144, 128), (1, 512, 1024, 256)]
 
 
 @pytest.mark.parametrize("prec", ["int8", "int8_kn", "int4", "fp16", "fp16_nk", "fp16acc"])
