@@ -458,6 +458,10 @@ def extras():
     out = {}
 
     def time_fn(fn, iters):
+        # every configuration starts from an idle GPU: without the pause, one
+        # timed right after a long power-capped loop inherits its clocks
+        torch.cuda.synchronize()
+        time.sleep(0.5)
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
