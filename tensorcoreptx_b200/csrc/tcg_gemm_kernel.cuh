@@ -561,41 +561,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t idesc = t < p.split_from ? p.idesc : p.idesc_half;
             const int acc = local % T::kAccBufs;
             const uint32_t acc_phase = (local / T::kAccBufs) & 1;
-            if (!wait_bounded(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, p.timeout_ns,
-                              (blockIdx.x << 8) | 0x20u | acc)) {
-                aborted = true;
-                break;
-            }
-            tc_fence_after();
             const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);  // wide: acc == 0
-            for (int kb = 0; kb < p.num_kb; ++kb) {
-                if (!wait_bounded(smem_u32(&full[stage]), phase, abort_flag, p.timeout_ns,
-                                  (blockIdx.x << 8) | 0x30u | stage)) {
-                    aborted = true;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t a_addr = stage0 + stage * T::kStageBytes;
+            // the MMAs of ring stage `st` (k-block kb) into accumulator half 0
+            // (bit 0 of `halves`) and, for two-block shapes, half 1 (bit 1)
+            const auto issue = [&](int st, int kb, int halves) {
+                const uint32_t a_addr = stage0 + st * T::kStageBytes;
                 const uint32_t b_addr = a_addr + T::kABytes;
 #pragma unroll
                 for (int k = 0; k < T::kKSteps; ++k) {
-                    const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
                     const uint64_t bdesc =
                         kBMn ? smem_desc_sw128(b_addr + k * T::kUmmaK * kBKBytes, T::kBoxBytesMn, 1024)
                              : smem_desc_sw128(b_addr + k * 32, 16, 1024);
-                    if constexpr (kPair) {
-                        umma_pair<kKind>(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
-                        if constexpr (kWide)  // each CTA's rows 128..255 into the second accumulator
-                            umma_pair<kKind>(d_tmem + kBN,
-                                             smem_desc_sw128(a_addr + T::kASubBytes + k * 32, 16, 1024), bdesc,
-                                             idesc, (kb | k) != 0 ? 1u : 0u);
-                    } else {
-                        umma<kKind>(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
-                        if constexpr (kWide)  // rows 128..255 of the tile into the second half
-                            umma<kKind>(d_tmem + kBN, smem_desc_sw128(a_addr + T::kASubBytes + k * 32, 16, 1024),
-                                        bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+                    const uint32_t accum = (kb | k) != 0 ? 1u : 0u;
+#pragma unroll
+                    for (int h = 0; h < T::kASub; ++h) {
+                        if (!(halves & (1 << h))) continue;
+                        const uint64_t adesc = smem_desc_sw128(a_addr + h * T::kASubBytes + k * 32, 16, 1024);
+                        if constexpr (kPair)
+                            umma_pair<kKind>(d_tmem + h * kBN, adesc, bdesc, idesc, accum);
+                        else
+                            umma<kKind>(d_tmem + h * kBN, adesc, bdesc, idesc, accum);
                     }
                 }
+            };
+            const auto release_stage = [&]() {
                 if constexpr (kPair)
                     umma_commit_pair(smem_u32(&empty[stage]), 0x3);
                 else
@@ -604,6 +593,58 @@ __global__ void __launch_bounds__(kThreads, 1)
                     stage = 0;
                     phase ^= 1u;
                 }
+            };
+            // accumulator (half 0 for two-block shapes) released by the epilogue
+            if (!wait_bounded(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, p.timeout_ns,
+                              (blockIdx.x << 8) | 0x20u | acc)) {
+                aborted = true;
+                break;
+            }
+            tc_fence_after();
+            int kb0 = 0;
+            if constexpr (kWide) {
+                // Two-block shapes keep one tile in TMEM.  The epilogue frees
+                // half 0 first; the first ring-full of k-blocks goes into half
+                // 0 while half 1 is still being read, then the same k-blocks
+                // into half 1 (each half still accumulates in k order).
+                const int pre = p.num_kb < kStages ? p.num_kb : kStages;
+                int st = stage;
+                uint32_t ph = phase;
+                for (int kb = 0; kb < pre; ++kb) {
+                    if (!wait_bounded(smem_u32(&full[st]), ph, abort_flag, p.timeout_ns,
+                                      (blockIdx.x << 8) | 0x30u | st)) {
+                        aborted = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue(st, kb, 1);
+                    if (++st == kStages) {
+                        st = 0;
+                        ph ^= 1u;
+                    }
+                }
+                if (aborted) break;
+                if (!wait_bounded(smem_u32(&tempty[1]), acc_phase ^ 1u, abort_flag, p.timeout_ns,
+                                  (blockIdx.x << 8) | 0x21u)) {
+                    aborted = true;
+                    break;
+                }
+                tc_fence_after();
+                for (int kb = 0; kb < pre; ++kb) {
+                    issue(stage, kb, 2);
+                    release_stage();
+                }
+                kb0 = pre;
+            }
+            for (int kb = kb0; kb < p.num_kb; ++kb) {
+                if (!wait_bounded(smem_u32(&full[stage]), phase, abort_flag, p.timeout_ns,
+                                  (blockIdx.x << 8) | 0x30u | stage)) {
+                    aborted = true;
+                    break;
+                }
+                tc_fence_after();
+                issue(stage, kb, 3);
+                release_stage();
             }
             if (aborted) break;
             if constexpr (kPair)
@@ -618,6 +659,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!wait_bounded(smem_u32(&tempty[acc]), ((local / T::kAccBufs) & 1) ^ 1u, abort_flag, p.timeout_ns,
                               (blockIdx.x << 8) | 0x60u | acc))
                 break;
+            if constexpr (kWide) {  // and the second half
+                if (!wait_bounded(smem_u32(&tempty[1]), (local & 1) ^ 1u, abort_flag, p.timeout_ns,
+                                  (blockIdx.x << 8) | 0x61u))
+                    break;
+            }
         }
     } else if (warp >= 2) {
         // ---------------------------------------------------- epilogue ----
@@ -670,9 +716,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                     static_cast<uint32_t>((acc + h) * kBN);
             if (p.tma_store) {
-                if (row0 >= p.M) continue;  // warp-uniform: all 32 rows below the matrix
 #pragma unroll 1
-                for (int c = 0; c < ncols; c += 64) {
+                for (int c = 0; c < ncols && row0 < p.M; c += 64) {  // (row0: warp-uniform)
                     const int col = col0 + c;
                     if (col >= p.N) break;  // warp-uniform
                     uint32_t va[32], vb[32];
@@ -690,8 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ++nstore;
                     }
                 }
-                continue;
-            }
+            } else {
 #pragma unroll 1
             for (int c = 0; c < ncols; c += 32) {
                 const int col = col0 + c;
@@ -730,14 +774,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();  // the tile is rewritten by the next 32 columns
             }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                const uint32_t tb = tempty_leader0 + static_cast<uint32_t>(acc * sizeof(uint64_t));
-                if constexpr (kPair)
-                    mbar_arrive_cluster(tb);
-                else
-                    mbar_arrive(tb);
+            if constexpr (kWide) {
+                // two-block shapes release each accumulator half as soon as
+                // it is read: the next tile's MMAs start on half 0 meanwhile
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    const uint32_t tb = tempty_leader0 + static_cast<uint32_t>(h * sizeof(uint64_t));
+                    if constexpr (kPair)
+                        mbar_arrive_cluster(tb);
+                    else
+                        mbar_arrive(tb);
+                }
+            }
+            }
+            if constexpr (!kWide) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    const uint32_t tb = tempty_leader0 + static_cast<uint32_t>(acc * sizeof(uint64_t));
+                    if constexpr (kPair)
+                        mbar_arrive_cluster(tb);
+                    else
+                        mbar_arrive(tb);
+                }
             }
         }
         // the staging tiles are read before the CTA exits (and its shared
