@@ -2,9 +2,9 @@
 //
 // Plays the role of the reference's solver*.cu + per-kernel launch_kernel
 // (src/solver.cu:6-28, kernels/*.cu launch wrappers): validates the problem,
-// picks the tile width, encodes the TMA descriptors and launches the
-// persistent tcgen05 kernel on the caller's stream.  Unlike the reference it
-// never exits the process: every failure is a tcg_status.
+// picks the tile shape and schedule, encodes the TMA descriptors and launches
+// the tcgen05 kernel on the caller's stream.  Unlike the reference it never
+// exits the process: every failure is a tcg_status.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -155,7 +155,7 @@ tcg_status encode_3d_uncached(CUtensorMap* map, CUtensorMapDataType dt, const vo
 // use that pair-wide tile.  Below that the candidates are CTA-pair 256 x BN
 // tiles (BN 256/128, one pair per two SMs) and single-CTA 128 x BN tiles
 // (BN 256/128/64, one per SM), with
-// cost = waves of persistent units x BN / efficiency, the critical path in
+// cost = waves of resident units x BN / efficiency, the critical path in
 // units of one SM's 128-column share of a tile, where efficiency is the
 // measured per-SM throughput of the shape relative to the 256 x 256 pair
 // (int8 on B200, 4096..16384 cubed: the pair reads a third less operand data
@@ -370,7 +370,7 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
         cfg.numAttrs = 1;
-        // persistent grid: no more pairs than can be resident at once
+        // pairs resident at once: the wave size, and the grid of a static schedule
         static int max_clusters[kMaxDevices] = {0};
         if (max_clusters[dev_id] == 0) {
             int n = 0;
