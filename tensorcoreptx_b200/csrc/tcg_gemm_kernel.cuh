@@ -47,7 +47,7 @@ struct GemmParams {
     int M, N, K, batches;
     int tiles_m, tiles_n, num_kb;
     int group_m;               // tile-rows per rasterisation band
-    int k_alternate;           // odd tiles of a unit walk K backwards (exact kinds only)
+    int k_alternate;           // work items of odd waves walk K backwards (exact kinds only)
     int l2_a, l2_b;            // L2 eviction priority of A / B loads (l2_policy), -1 = no hint
     int n_extra;               // further destinations of C (peer GPUs' buffers), <= kMaxExtraDst
     void* extra[7];            // each receives the same tile at the same offset as C
@@ -150,14 +150,16 @@ __device__ __forceinline__ void record_failure(volatile uint32_t* abort_flag, ui
               (static_cast<unsigned long long>(kErrWaitTimeout) << 32) | detail);
 }
 
-// Single-thread bounded wait.  true: the phase of `parity` completed.
-// false: this CTA is aborting (this wait expired, or another role's did).
+// One try_wait; kClusterScope: acquire at cluster scope (data written into
+// this CTA's shared memory by the other CTA of its cluster).
 template <bool kClusterScope = false>
 __device__ __forceinline__ bool try_wait_scoped(uint32_t bar, uint32_t parity)
 {
     return kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
 }
 
+// Single-thread bounded wait.  true: the phase of `parity` completed.
+// false: this CTA is aborting (this wait expired, or another role's did).
 template <bool kClusterScope = false>
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
                                              unsigned long long timeout_ns, uint32_t detail)
@@ -431,11 +433,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t tx = half < 0 ? T::kTxBytes : T::kTxBytes - (kPair ? 2 : 1) * (T::kBBytes / 2);
             const int b_atoms = half < 0 ? T::kBRows / T::kAtomN : T::kBRows / T::kAtomN / 2;
             const CUtensorMap* mapB = half < 0 ? &tmB : &tmBh;
-            // Units advance through their tiles in step, so the whole grid
-            // finishes a wave of tiles at about the same K.  Walking K
-            // backwards on every other wave starts each wave on the K range
-            // the previous wave just brought into L2.  Integer accumulation is
-            // exact in any order; floating-point kinds keep one order.
+            // The items in flight (about one wave: wave_units consecutive
+            // items) finish at about the same K.  Walking K backwards on every
+            // other wave starts each wave on the K range the previous wave just
+            // brought into L2.  Integer accumulation is exact in any order;
+            // floating-point kinds keep one order.
             const bool reverse = p.k_alternate && ((t / p.wave_units) & 1);
             for (int kb = 0; kb < p.num_kb; ++kb) {
                 const int kc = reverse ? p.num_kb - 1 - kb : kb;
