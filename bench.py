@@ -510,6 +510,50 @@ def extras():
             out[f"fp16_{n}_torch_matmul"] = {"tflops": 2 * n ** 3 / ms_lib / 1e9, "ms": ms_lib}
         del A, B
     torch.cuda.empty_cache()
+    # the rows beyond the benchmark configurations: FP8, the fused dequant
+    # epilogue, on-device quantisation and the batched entry
+    n = 4096
+    for n8 in (4096, 8192):
+        A8 = (torch.rand(n8, n8, generator=g, device=dev) * 2 - 1).to(torch.float8_e4m3fn)
+        B8 = (torch.rand(n8, n8, generator=g, device=dev) * 2 - 1).to(torch.float8_e4m3fn)
+        ms = time_fn(lambda: T.gemm_fp8(A8, B8), 20)
+        out[f"fp8_e4m3_{n8}"] = {"tflops": 2 * n8 ** 3 / ms / 1e9, "ms": ms}
+        try:
+            one = torch.ones(1, device=dev)
+            ms_lib = time_fn(lambda: torch._scaled_mm(A8, B8.t(), scale_a=one, scale_b=one,
+                                                      out_dtype=torch.float32), 20)
+            out[f"fp8_e4m3_{n8}_torch_scaled_mm"] = {"tflops": 2 * n8 ** 3 / ms_lib / 1e9, "ms": ms_lib}
+        except Exception as e:  # pragma: no cover
+            out[f"fp8_e4m3_{n8}_torch_scaled_mm"] = {"error": str(e)[:80]}
+        del A8, B8
+    Af = torch.randn(n, n, generator=g, device=dev)
+    Bf = torch.randn(n, n, generator=g, device=dev)
+    qa, sa = T.quantize_absmax_int8(Af)
+    qb, sb = T.quantize_absmax_int8(Bf)
+    ms = time_fn(lambda: T.gemm_int8_dequant(qa, qb, sa, sb), 50)
+    out["int8_4096_dequant_fused"] = {"tops": 2 * n ** 3 / ms / 1e9, "ms": ms}
+    ms = time_fn(lambda: T.gemm_int8(qa, qb).float() * (sa * sb), 50)
+    out["int8_4096_then_torch_dequant"] = {"tops": 2 * n ** 3 / ms / 1e9, "ms": ms}
+    del Af, Bf, qa, qb
+    # quantisation: HBM-bound; algorithmic bytes = fp32 read once + codes
+    # written (int8: 5 bytes per value, int4: 4.5); 256 MB of fp32, beyond L2
+    hbm = float(load_peaks()[0].get("hbm_gbs", 6650.0))
+    Xq = torch.randn(8192, 8192, generator=g, device=dev)
+    for name, fn, per in (("quantize_int8_8192x8192", lambda: T.quantize_absmax_int8(Xq), 5.0),
+                          ("quantize_int4_8192x8192", lambda: T.quantize_absmax_int4(Xq), 4.5)):
+        ms = time_fn(fn, 20)
+        gbs = per * Xq.numel() / ms / 1e6
+        out[name] = {"gbs": gbs, "ms": ms, "frac_hbm": gbs / hbm}
+    del Xq
+    # batched: the reference profiles num_batches = 4
+    Ab = (torch.rand(4, 2048, 2048, generator=g, device=dev) * 2 - 1).half()
+    Bb = (torch.rand(4, 2048, 2048, generator=g, device=dev) * 2 - 1).half()
+    ms = time_fn(lambda: T.gemm_fp16(Ab, Bb), 30)
+    out["fp16_batched_4x2048"] = {"tflops": 4 * 2 * 2048 ** 3 / ms / 1e9, "ms": ms}
+    ms_lib = time_fn(lambda: torch.bmm(Ab, Bb), 30)
+    out["fp16_batched_4x2048_torch_bmm"] = {"tflops": 4 * 2 * 2048 ** 3 / ms_lib / 1e9, "ms": ms_lib}
+    del Ab, Bb
+    torch.cuda.empty_cache()
     # the smallest configuration (fp16 512^3) is launch-bound from Python;
     # its device time, from 20 launches replayed in a CUDA graph
     n = 512
