@@ -896,31 +896,39 @@ struct UnpackSeg {
     int tail;
 };
 
-__device__ __forceinline__ void unpack_chunk(const UnpackSeg& s, long long i)
+__device__ __forceinline__ uint4 unpack_load(const UnpackSeg& s0, const UnpackSeg& s1, long long i)
 {
-    const uint4 v = s.in[i];
+    return i < s0.n16 ? s0.in[i] : s1.in[i - s0.n16];
+}
+
+__device__ __forceinline__ void unpack_store(const UnpackSeg& s0, const UnpackSeg& s1, long long i, uint4 v)
+{
     uint4 a, b;
     widen_word(v.x, a.x, a.y);
     widen_word(v.y, a.z, a.w);
     widen_word(v.z, b.x, b.y);
     widen_word(v.w, b.z, b.w);
-    s.out[2 * i] = a;
-    s.out[2 * i + 1] = b;
+    uint4* out = i < s0.n16 ? s0.out + 2 * i : s1.out + 2 * (i - s0.n16);
+    out[0] = a;
+    out[1] = b;
 }
 
+// Four chunks per thread per step, all four loads issued before any store.
 __global__ void unpack_s4_kernel(const UnpackSeg s0, const UnpackSeg s1)
 {
     grid_dependency_wait();
     grid_launch_dependents();
     const long long total = s0.n16 + s1.n16;
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += 2 * stride) {
-        const long long j = i + stride;
-        if (i < s0.n16) unpack_chunk(s0, i); else unpack_chunk(s1, i - s0.n16);
-        if (j < total) {
-            if (j < s0.n16) unpack_chunk(s0, j); else unpack_chunk(s1, j - s0.n16);
-        }
+    long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (; i + 3 * stride < total; i += 4 * stride) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = unpack_load(s0, s1, i + u * stride);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) unpack_store(s0, s1, i + u * stride, v[u]);
     }
+    for (; i < total; i += stride) unpack_store(s0, s1, i, unpack_load(s0, s1, i));
     if (blockIdx.x == 0) {
         const UnpackSeg& s = threadIdx.x < 16 ? s0 : s1;
         const int k = threadIdx.x & 15;

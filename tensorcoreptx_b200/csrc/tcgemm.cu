@@ -501,7 +501,7 @@ tcg_status launch_unpack(const int8_t* in0, int8_t* out0, size_t n0, const int8_
     const UnpackSeg s0 = unpack_seg(in0, out0, n0);
     const UnpackSeg s1 = n1 ? unpack_seg(in1, out1, n1) : unpack_seg(in0, out0, 0);
     const long long chunks = s0.n16 + s1.n16;
-    long long blocks = (chunks + 511) / 512;  // two chunks per thread
+    long long blocks = (chunks + 1023) / 1024;  // four chunks per thread
     const long long cap = static_cast<long long>(sms) * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
@@ -733,7 +733,7 @@ static tcg_status quantize_common(const float* src, int8_t* dst, long long n, lo
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaMemsetAsync(scale, 0, sizeof(float), st);
     if (e != cudaSuccess) return cuda_fail(e);
-    const long long cap = static_cast<long long>(dev->sms) * 4;
+    const long long cap = static_cast<long long>(dev->sms) * 8;
     long long blocks = (n / 4 + 255) / 256;
     blocks = blocks < 1 ? 1 : (blocks > cap ? cap : blocks);
     absmax_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(src, n, reinterpret_cast<int*>(scale));

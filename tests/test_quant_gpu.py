@@ -21,7 +21,7 @@ def T():
     return t
 
 
-@pytest.mark.parametrize("n", [1, 3, 4, 1000, 4097, 1 << 20])
+@pytest.mark.parametrize("n", [1, 3, 4, 1000, 4097, 1 << 20, (1 << 24) + 3])
 def test_quantize_int8_bit_exact(n):
     rng = np.random.default_rng(n)
     x = (rng.standard_normal(n) * 3).astype(np.float32)
@@ -31,7 +31,7 @@ def test_quantize_int8_bit_exact(n):
     assert np.float32(s.item()).view(np.uint32) == np.float32(so).view(np.uint32)
 
 
-@pytest.mark.parametrize("rows,k", [(1, 2), (3, 10), (512, 512), (77, 130)])
+@pytest.mark.parametrize("rows,k", [(1, 2), (3, 10), (512, 512), (77, 130), (2048, 4098)])
 def test_quantize_int4_bit_exact(rows, k):
     rng = np.random.default_rng(rows * k)
     x = (rng.standard_normal((rows, k)) * 2).astype(np.float32)
