@@ -283,11 +283,19 @@ def run_ours(args):
                              nat.TCG_B_NK, stream.cuda_stream)
         nat.check("tcg_gemm_s8", st)
 
+    # --gather nccl: block-cyclic row blocks, each multiplied into its place
+    # in the full C and all-gathered in place while the next one multiplies
+    nccl_chunks = 4
+    if gather == "nccl" and rows % nccl_chunks:
+        raise SystemExit("--gather nccl needs each rank's rows to split into 4 blocks")
+
     def step():
-        gemm_launch()
-        if C_full is not None:
+        if gather == "nccl":
+            from tensorcoreptx_b200.dist import gathered_gemm_int8
             with torch.cuda.stream(stream):
-                dist.all_gather_into_tensor(C_full, C)
+                gathered_gemm_int8(A, BT, nccl_chunks, out=C_full)
+            return
+        gemm_launch()
 
     clocks = ClockSampler(list(range(world)) if rank == 0 else [local])
     if rank == 0:
@@ -309,12 +317,10 @@ def run_ours(args):
     t_end = torch.cuda.Event(enable_timing=True)
     t_begin.record(stream)
     for i in range(args.steps):
+        # with a gather the bracket holds the whole step (GEMM and transfer)
         ev[i][0].record(stream)
-        gemm_launch()
+        step()
         ev[i][1].record(stream)
-        if C_full is not None:
-            with torch.cuda.stream(stream):
-                dist.all_gather_into_tensor(C_full, C)
     t_end.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -394,7 +400,9 @@ def run_ours(args):
             "data": "synthetic",
             "config": {
                 "workload": f"int8 GEMM M=N=K={size}, A row-sharded over {world} GPU(s), "
-                            f"B replicated, int32 C" + {"none": "", "nccl": ", C all-gathered (NCCL)",
+                            f"B replicated, int32 C" + {"none": "", "nccl": ", C all-gathered (NCCL, block-cyclic rows, "
+                                                                 "4 blocks each gathered while the next "
+                                                                 "multiplies)",
                                                          "p2p": ", C all-gathered by the GEMM epilogue "
                                                                 "over NVLink peer stores"}[gather],
                 "per_rank": f"{rows}x{size}x{size}",
@@ -416,7 +424,7 @@ def run_ours(args):
             },
             "e2e": {"value": ops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * (nccl_chunks if gather == "nccl" else 1),
             "clocks": clocks.summary("kernel"),
             "clocks_e2e": clocks.summary("e2e"),
         }

@@ -66,6 +66,67 @@ def sharded_gemm_int8(A_local: torch.Tensor, BT: torch.Tensor, gather: bool = Fa
     return out
 
 
+def cyclic_row_blocks(M: int, world: int, rank: int, chunks: int) -> list[tuple[int, int]]:
+    """Block-cyclic row shards: the M rows are `chunks` groups of `world`
+    blocks of M / (chunks * world) rows; `rank` owns block `rank` of every
+    group.  Returns its [r0, r1) blocks in order (its local rows, stacked)."""
+    if world < 1 or not 0 <= rank < world or chunks < 1:
+        raise ValueError("bad rank / world size / chunk count")
+    if M % (chunks * world):
+        raise ValueError("block-cyclic shards need M divisible by chunks x world")
+    ch = M // (chunks * world)
+    return [(c * world * ch + rank * ch, c * world * ch + (rank + 1) * ch) for c in range(chunks)]
+
+
+def gathered_gemm_int8(A_local: torch.Tensor, BT: torch.Tensor, chunks: int, out: Optional[torch.Tensor] = None,
+                       group=None, local_gemm_into: Optional[Callable] = None) -> torch.Tensor:
+    """Full C = A x BT^T on every rank, the all-gather overlapped with the
+    GEMM.  A is sharded block-cyclically (``cyclic_row_blocks``): A_local
+    stacks this rank's `chunks` row blocks.  Block c is multiplied straight
+    into its rows of the full C, then gathered by an in-place all-gather of
+    row group c (contiguous, because every rank's block c sits in it), which
+    runs while block c+1 is multiplied.
+
+    `local_gemm_into(A_rows, BT, C_rows)` writes A_rows x BT^T into the
+    contiguous int32 view C_rows; it defaults to the tensor-core GEMM on the
+    current stream.
+    """
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    rows, K = A_local.shape
+    N = BT.shape[0]
+    if rows % chunks:
+        raise RuntimeError("A_local rows must split into `chunks` equal blocks")
+    ch = rows // chunks
+    if out is None:
+        out = torch.empty((rows * world, N), dtype=torch.int32, device=A_local.device)
+    if out.shape != (rows * world, N) or not out.is_contiguous():
+        raise RuntimeError("out must be a contiguous (world x local rows) x N int32 tensor")
+    if local_gemm_into is None:
+        local_gemm_into = _gemm_int8_into
+    works = []
+    for c in range(chunks):
+        group_rows = out[c * world * ch:(c + 1) * world * ch]
+        mine = group_rows[rank * ch:(rank + 1) * ch]
+        local_gemm_into(A_local[c * ch:(c + 1) * ch], BT, mine)
+        works.append(dist.all_gather_into_tensor(group_rows, mine, group=group, async_op=True))
+    for w in works:
+        w.wait()
+    return out
+
+
+def _gemm_int8_into(A_rows: torch.Tensor, BT: torch.Tensor, C_rows: torch.Tensor):
+    """C_rows = A_rows x BT^T with the tensor-core GEMM on the current stream."""
+    from . import _native as nat
+    from .gemm import _check, _stream_ptr
+    _check(A_rows.is_contiguous() and BT.is_contiguous() and C_rows.is_contiguous(),
+           "operands must be contiguous")
+    M, K = A_rows.shape
+    st = nat.lib().tcg_gemm_s8(A_rows.data_ptr(), BT.data_ptr(), C_rows.data_ptr(), M, BT.shape[0], K, 1,
+                               nat.TCG_B_NK, _stream_ptr(A_rows))
+    nat.check("gathered_gemm_int8", st)
+
+
 class PeerGather:
     """All-gather of row-sharded C through the GEMM epilogue.
 

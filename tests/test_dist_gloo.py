@@ -15,7 +15,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from tensorcoreptx_b200.dist import max_over_ranks, shard_rows, sharded_gemm_int8
+from tensorcoreptx_b200.dist import (cyclic_row_blocks, gathered_gemm_int8, max_over_ranks, shard_rows,
+                                     sharded_gemm_int8)
 
 
 def _free_port():
@@ -66,6 +67,54 @@ def test_shard_rows_partition():
     assert [shard_rows(32768, 8, r) for r in range(8)] == [(r * 4096, (r + 1) * 4096) for r in range(8)]
     with pytest.raises(ValueError):
         shard_rows(10, 2, 2)
+
+
+def test_cyclic_row_blocks_partition():
+    for world in (1, 2, 3, 8):
+        for chunks in (1, 2, 4):
+            M = world * chunks * 16
+            blocks = sorted(b for r in range(world) for b in cyclic_row_blocks(M, world, r, chunks))
+            assert blocks[0][0] == 0 and blocks[-1][1] == M
+            for (a0, a1), (b0, b1) in zip(blocks, blocks[1:]):
+                assert a1 == b0 and a1 - a0 == M // (world * chunks)
+    assert cyclic_row_blocks(32, 2, 1, 2) == [(8, 16), (24, 32)]
+    with pytest.raises(ValueError):
+        cyclic_row_blocks(30, 2, 0, 4)
+
+
+def _cpu_gemm_into(A_rows, BT, C_rows):
+    C_rows.copy_(_cpu_gemm(A_rows, BT))
+
+
+def _worker_overlap(rank, world, port, M, N, K, chunks, q):
+    try:
+        _init(rank, world, port)
+        rng = np.random.default_rng(1)  # same full inputs on every rank
+        A = torch.from_numpy(rng.integers(-128, 128, (M, K), dtype=np.int8))
+        BT = torch.from_numpy(rng.integers(-128, 128, (N, K), dtype=np.int8))
+        A_local = torch.cat([A[r0:r1] for r0, r1 in cyclic_row_blocks(M, world, rank, chunks)]).contiguous()
+        C = gathered_gemm_int8(A_local, BT, chunks, local_gemm_into=_cpu_gemm_into)
+        ok = bool(torch.equal(C, _cpu_gemm(A, BT)))
+        dist.destroy_process_group()
+        q.put((rank, ok, ""))
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, False, repr(e)))
+
+
+@pytest.mark.parametrize("world,chunks", [(2, 4), (3, 2)])
+def test_overlapped_gather_assembles_full_c(world, chunks):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    M, N, K = world * chunks * 8, 40, 32
+    procs = [ctx.Process(target=_worker_overlap, args=(r, world, port, M, N, K, chunks, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok, err in sorted(results):
+        assert ok, (rank, err)
 
 
 @pytest.mark.parametrize("world", [2])

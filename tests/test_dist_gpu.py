@@ -1,5 +1,7 @@
 """Row-sharded GEMM over NCCL on 2 GPUs (skipped with fewer GPUs): every
-rank's gathered C equals the single-GPU product of the full matrices."""
+rank's gathered C -- one all-gather after the GEMM, block-cyclic blocks
+gathered while the next multiplies, and the GEMM epilogue's peer stores --
+equals the single-GPU product of the full matrices."""
 import os
 import socket
 
@@ -38,6 +40,12 @@ def _worker(rank, world, port, q):
         C = sharded_gemm_int8(A[r0:r1].contiguous(), BT, gather=True)
         full = T.gemm_int8(A, BT)
         ok = bool(torch.equal(C, full))
+        # block-cyclic shards, each block gathered while the next multiplies
+        from tensorcoreptx_b200.dist import cyclic_row_blocks, gathered_gemm_int8
+        A_cyc = torch.cat([A[b0:b1] for b0, b1 in cyclic_row_blocks(M, world, rank, 4)]).contiguous()
+        Cg = gathered_gemm_int8(A_cyc, BT, 4)
+        torch.cuda.synchronize()
+        ok = ok and bool(torch.equal(Cg, full))
         # the same gather through the GEMM epilogue over peer memory, twice
         from tensorcoreptx_b200.dist import PeerGather
         with PeerGather(M, N, dev) as pg:
