@@ -577,3 +577,15 @@ def test_host_pipeline_matches_device_path(M, N, K, chunks):
     torch.cuda.current_stream().synchronize()
     ref = T.gemm_fp16(Ah.cuda(), Bh.cuda()).cpu()
     assert torch.equal(Cf, ref)
+
+
+@pytest.mark.parametrize("argv", [["gemm_int8", "--m", "512", "--n", "256", "--k", "128"],
+                                  ["gemm_int4", "--m", "256", "--n", "256", "--k", "256"],
+                                  ["gemm_fp16", "--m", "256", "--n", "256", "--k", "128", "--acc", "fp16"],
+                                  ["gemm_fp8", "--m", "256", "--n", "256", "--k", "128"],
+                                  ["gemm_int8_dequant", "--m", "256", "--n", "256", "--k", "128"],
+                                  ["quantize_int4", "--m", "64", "--k", "64"]])
+def test_opbench_runs(argv, capsys):
+    from tensorcoreptx_b200 import opbench
+    opbench.main(argv + ["--iters", "2", "--warmup", "1"])
+    assert "per call" in capsys.readouterr().out
