@@ -55,7 +55,7 @@ struct GemmParams {
     const float* scale_a;      // non-null (int kinds): C = float(acc) * (*scale_a * *scale_b)
     const float* scale_b;
     int vec_store;             // C rows 16-byte aligned (N % 4 == 0, C aligned)
-    int tma_store;             // write C through the tensor map (vec_store and no peer destinations)
+    int tma_store;             // write C through the tensor map (vec_store; peers then get plain stores)
     int split_from;            // work items from here on are column halves of the last tiles
     uint32_t idesc_half;       // instruction descriptor of a half (N = kBN / 2)
     int dynamic;               // 1: one cluster per work item, taken over by cluster launch control
@@ -258,6 +258,28 @@ __device__ __forceinline__ void epi_store_tma(const CUtensorMap* tmC, uint32_t* 
     if (lane == 0) {
         tma_store_3d(tmC, buf_s, col, row, b);
         bulk_commit_group();
+    }
+}
+
+// The same 32 x 32 block, read back from its staging tile, to every peer
+// destination (the epilogue all-gather): plain 16-byte stores over NVLink,
+// 4 rows x 128 bytes per instruction.  C rows are 16-byte aligned here.
+__device__ __forceinline__ void epi_store_peers(const GemmParams& p, const uint32_t* buf, int row0, int col,
+                                                long long cbase, int lane)
+{
+    const int rsub = lane >> 3;
+    const int gcol = col + (lane & 7) * 4;
+#pragma unroll 2
+    for (int it = 0; it < 8; ++it) {
+        const int r = it * 4 + rsub;
+        const uint4 w = *reinterpret_cast<const uint4*>(buf + r * 32 + (((lane & 7) ^ (r & 7)) << 2));
+        const int grow = row0 + r;
+        if (grow < p.M && gcol < p.N) {
+            const long long off = cbase + static_cast<long long>(grow) * p.N + gcol;
+#pragma unroll 1
+            for (int d = 0; d < p.n_extra; ++d)
+                *reinterpret_cast<uint4*>(static_cast<uint32_t*>(p.extra[d]) + off) = w;
+        }
     }
 }
 
@@ -730,10 +752,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     epi_convert<kAccF16>(vb, dequant, combined);
                     epi_store_tma(&tmC, stile + (nstore & 1u) * 1024, stile_s + (nstore & 1u) * 4096, va, lane,
                                   col, row0, b);
+                    if (p.n_extra > 0) epi_store_peers(p, stile + (nstore & 1u) * 1024, row0, col, cbase, lane);
                     ++nstore;
                     if (c + 32 < ncols && col + 32 < p.N) {
                         epi_store_tma(&tmC, stile + (nstore & 1u) * 1024, stile_s + (nstore & 1u) * 4096, vb,
                                       lane, col + 32, row0, b);
+                        if (p.n_extra > 0)
+                            epi_store_peers(p, stile + (nstore & 1u) * 1024, row0, col + 32, cbase, lane);
                         ++nstore;
                     }
                 }

@@ -337,9 +337,10 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     for (int i = 0; i < n_extra; ++i)  // every destination must take 16-byte stores like C
         if ((reinterpret_cast<uintptr_t>(extra[i]) & 15u) != 0) p.vec_store = 0;
     // C through a tensor map (32 x 32 word boxes, 128-byte swizzle) when its
-    // rows are 16-byte aligned and there are no peer destinations
+    // rows (and every peer destination) are 16-byte aligned; peer copies are
+    // then plain stores from the same staging tile
     static const int env_tma_store = env_int("TCG_TMA_STORE", 1);
-    p.tma_store = (env_tma_store && p.vec_store && n_extra == 0) ? 1 : 0;
+    p.tma_store = (env_tma_store && p.vec_store) ? 1 : 0;
     CUtensorMap mC;
     std::memset(&mC, 0, sizeof mC);
     if (p.tma_store) {

@@ -589,3 +589,25 @@ def test_opbench_runs(argv, capsys):
     from tensorcoreptx_b200 import opbench
     opbench.main(argv + ["--iters", "2", "--warmup", "1"])
     assert "per call" in capsys.readouterr().out
+
+
+@pytest.mark.parametrize("M,N,K", [(3328, 2560, 256), (300, 520, 128), (257, 130, 64)])
+def test_multi_destination_epilogue_on_one_gpu(M, N, K):
+    """tcg_gemm_s8_multi with two further destinations on the same GPU (the
+    epilogue all-gather's path, peers replaced by local buffers): C through
+    the TMA store when its rows are 16-byte aligned (N % 4 == 0) and plain
+    stores otherwise, every destination receiving the whole product."""
+    import ctypes as C
+    from tensorcoreptx_b200 import _native as nat
+    rng = np.random.default_rng(M + N)
+    A, BT = rand_s8(rng, (M, K)), rand_s8(rng, (N, K))
+    dA, dB = _cuda(A), _cuda(BT)
+    outs = [torch.full((M, N), -7, dtype=torch.int32, device=DEV) for _ in range(3)]
+    dsts = (C.c_void_p * 3)(*[o.data_ptr() for o in outs])
+    st = nat.lib().tcg_gemm_s8_multi(dA.data_ptr(), dB.data_ptr(), dsts, 3, M, N, K, nat.TCG_B_NK,
+                                     torch.cuda.current_stream().cuda_stream)
+    nat.check("tcg_gemm_s8_multi", st)
+    torch.cuda.synchronize()
+    ref = O.gemm_s8(A, BT, threads=8)
+    for o in outs:
+        assert np.array_equal(o.cpu().numpy(), ref)
