@@ -17,7 +17,8 @@ def _rand_f8(g, shape, dt):
 @pytest.mark.parametrize("afmt,bfmt", [(torch.float8_e4m3fn, torch.float8_e4m3fn),
                                        (torch.float8_e5m2, torch.float8_e5m2),
                                        (torch.float8_e4m3fn, torch.float8_e5m2)])
-@pytest.mark.parametrize("M,N,K,layout", [(256, 256, 256, "nk"), (300, 144, 512, "kn"), (1024, 512, 1024, "nk")])
+@pytest.mark.parametrize("M,N,K,layout", [(256, 256, 256, "nk"), (300, 144, 512, "kn"), (1024, 512, 1024, "nk"),
+                                           (3328, 2560, 128, "nk")])
 def test_fp8_against_fp64(afmt, bfmt, M, N, K, layout):
     import tensorcoreptx_b200 as T
     g = torch.Generator(device=DEV).manual_seed(M + N + K)

@@ -81,7 +81,7 @@ def test_reference_quant_round_trip_on_device(prec):
     assert f"{acc.snr_db:.1f}" == k["snr_db"]
 
 
-@pytest.mark.parametrize("M,N,K", [(300, 200, 256), (1024, 2048, 512)])
+@pytest.mark.parametrize("M,N,K", [(300, 200, 256), (1024, 2048, 512), (3328, 2560, 128)])
 def test_dequant_epilogue_every_shape(M, N, K):
     rng = np.random.default_rng(M)
     A = rng.integers(-127, 128, (M, K), dtype=np.int8)
