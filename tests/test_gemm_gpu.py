@@ -562,7 +562,8 @@ def test_tail_split_multiwave(prec):
 
 # ------------------------------------------------------- host-buffer entry --
 
-@pytest.mark.parametrize("M,N,K,chunks", [(1000, 384, 256, 3), (200, 128, 64, 8), (2048, 512, 512, 8)])
+@pytest.mark.parametrize("M,N,K,chunks", [(1000, 384, 256, 3), (200, 128, 64, 8), (2048, 512, 512, 8),
+                                           (4096, 3072, 256, 8)])
 def test_host_pipeline_matches_device_path(M, N, K, chunks):
     T = tcg()
     rng = np.random.default_rng(M + N)
