@@ -5,7 +5,8 @@
 
 Operations: gemm_int8 (B given as BT, N x K), gemm_int8_kn, gemm_int4 (packed
 operands), gemm_fp16 (B K x N; --acc fp32|fp16), gemm_fp8 (e4m3, BT),
-gemm_int8_dequant, quantize_int8 / quantize_int4 (an M x K fp32 input).
+gemm_int8_dequant, quantize_int8 / quantize_int4 (an M x K fp32 input);
+reference points through torch: torch_int_mm, torch_matmul_fp16.
 Prints one line: the operation, its shape, the mean time per call after
 warm-up and the rate (TOPS / TFLOP/s for GEMMs, GB/s of algorithmic bytes for
 quantisation).  Also the workload for profiling a single kernel under ncu.
@@ -61,6 +62,12 @@ def main(argv=None):
         qa, sa = T.quantize_absmax_int8(torch.randn(M, K, generator=g, device=dev))
         qb, sb = T.quantize_absmax_int8(torch.randn(N, K, generator=g, device=dev))
         fn, work, unit = (lambda: T.gemm_int8_dequant(qa, qb, sa, sb)), gemm_ops, "TOPS"
+    elif a.op == "torch_int_mm":  # reference point: torch / cuBLASLt int8 GEMM, same inputs
+        A, B = s8(M, K), s8(N, K)
+        fn, work, unit = (lambda: torch._int_mm(A, B.t())), gemm_ops, "TOPS"
+    elif a.op == "torch_matmul_fp16":  # reference point: torch / cuBLAS fp16 GEMM
+        A, B = f16(M, K), f16(K, N)
+        fn, work, unit = (lambda: torch.matmul(A, B)), gemm_ops, "TFLOP/s"
     elif a.op in ("quantize_int8", "quantize_int4"):
         X = torch.randn(M, K, generator=g, device=dev)
         q = T.quantize_absmax_int8 if a.op == "quantize_int8" else T.quantize_absmax_int4
