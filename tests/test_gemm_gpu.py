@@ -612,3 +612,46 @@ def test_multi_destination_epilogue_on_one_gpu(M, N, K):
     ref = O.gemm_s8(A, BT, threads=8)
     for o in outs:
         assert np.array_equal(o.cpu().numpy(), ref)
+
+
+_MULTIWAVE = [("int8_kn", 1, 4096, 2560, 128), ("int8", 3, 2048, 2048, 128), ("int4", 1, 4096, 2560, 256),
+              ("fp16_nk", 1, 4096, 2560, 64), ("fp16", 3, 2048, 2048, 64), ("fp16acc", 1, 4096, 2560, 64)]
+
+
+@pytest.mark.parametrize("prec,bt,M,N,K", _MULTIWAVE, ids=[c[0] + f"_b{c[1]}" for c in _MULTIWAVE])
+def test_multiwave_layouts_and_batches(prec, bt, M, N, K):
+    """More than one wave of pair-wide tiles (cluster launch control,
+    batches folded into the work items) for each B layout, batch count and
+    precision: integers exact, fp16 within tolerance on sampled rows of
+    every batch."""
+    T = tcg()
+    rng = np.random.default_rng(M + N + K + bt)
+    shp = (lambda r, c: (bt, r, c)) if bt > 1 else (lambda r, c: (r, c))
+    if prec.startswith("int8"):
+        A = rand_s8(rng, shp(M, K))
+        B = rand_s8(rng, shp(K, N) if prec == "int8_kn" else shp(N, K))
+        C = (T.gemm_int8_kn if prec == "int8_kn" else T.gemm_int8)(_cuda(A), _cuda(B)).cpu().numpy()
+    elif prec == "int4":
+        A, B = rand_s4_packed(rng, M, K), rand_s4_packed(rng, N, K)
+        C = T.gemm_int4(_cuda(A), _cuda(B)).cpu().numpy()
+    else:
+        A = rand_f16_bits(rng, shp(M, K))
+        B = rand_f16_bits(rng, shp(N, K) if prec == "fp16_nk" else shp(K, N))
+        acc = "fp16" if prec == "fp16acc" else "fp32"
+        fn = T.gemm_fp16_nk if prec == "fp16_nk" else T.gemm_fp16
+        C = fn(_cuda(A, torch.float16), _cuda(B, torch.float16), acc=acc).cpu().numpy()
+    assert T.last_tile_m() == 512
+    for b in range(bt):
+        Ab = A[b] if bt > 1 else A
+        Bb = B[b] if bt > 1 else B
+        Cb = C[b] if bt > 1 else C
+        if prec == "int8":
+            assert np.array_equal(Cb, O.gemm_s8(Ab, Bb, threads=8))
+        elif prec == "int8_kn":
+            assert np.array_equal(Cb, O.gemm_s8_kn(Ab, Bb))
+        elif prec == "int4":
+            assert np.array_equal(Cb, O.gemm_s4(Ab, Bb, K, threads=8))
+        else:
+            for r0 in (0, M // 2 + 7, M - 1):
+                ref = O.gemm_f16_f64(Ab, Bb, b_kn=(prec != "fp16_nk"), row0=r0, rows=1)
+                assert np.abs(Cb[r0] - ref[r0]).max() <= f16_tol(Ab, Bb, K) * (8 if prec == "fp16acc" else 1)
