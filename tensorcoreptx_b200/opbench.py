@@ -17,6 +17,10 @@ import argparse
 import time
 
 
+OPS = ("gemm_int8", "gemm_int8_kn", "gemm_int4", "gemm_fp16", "gemm_fp8", "gemm_int8_dequant",
+       "quantize_int8", "quantize_int4", "torch_int_mm", "torch_matmul_fp16")
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("op")
@@ -27,6 +31,8 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args(argv)
+    if a.op not in OPS:
+        raise SystemExit(f"unknown operation {a.op!r}; one of {', '.join(OPS)}")
 
     import torch
     import tensorcoreptx_b200 as T

@@ -111,3 +111,9 @@ def test_host_block_schedule_covers_every_block_once_after_its_operands():
         assert sorted(mms) == [(i, j) for i in range(mc) for j in range(nc)]
         assert loaded == {("a", i) for i in range(mc)} | {("b", j) for j in range(nc)}
         assert steps[:3] == [("a", 0), ("b", 0), ("mm", 0, 0)]
+
+
+def test_opbench_rejects_unknown_operation_without_a_gpu():
+    from tensorcoreptx_b200 import opbench
+    with pytest.raises(SystemExit, match="unknown operation"):
+        opbench.main(["gemm_int9"])
