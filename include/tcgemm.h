@@ -140,13 +140,17 @@ tcg_status tcg_unpack_s4(const int8_t* packed, int8_t* out, size_t n_packed, voi
  * libtcgemm.so, TCG_S4_STATIC_SCRATCH_BYTES large, that every GPU which loads
  * the library holds until the process exits.
  *
- * Same operands, result and status codes as tcg_gemm_s4.  The scratch need
- * (tcg_gemm_s4_workspace_size(M, N, K, batches)) must not exceed
- * TCG_S4_STATIC_SCRATCH_BYTES: larger problems return TCG_ERR_WORKSPACE and
- * launch nothing (4096 x 4096 x 4096 fits exactly).  No cudaMalloc/cudaFree
- * or other allocating routine is called.  The first call on a device looks up
+ * Same operands, result and status codes as tcg_gemm_s4.  The limit is on
+ * the scratch need, tcg_gemm_s4_workspace_size(M, N, K, batches) <=
+ * TCG_S4_STATIC_SCRATCH_BYTES, i.e. batches*M*K + batches*N*K bytes (the
+ * widened A and B, each rounded up to 256 bytes) of at most 32 MiB: 4096 x
+ * 4096 x 4096 fits exactly, and so does 8192 x 8192 x 2048.  Larger problems
+ * return TCG_ERR_WORKSPACE and launch nothing.  No cudaMalloc/cudaFree or
+ * other allocating routine is called.  The first call on a device looks up
  * the array's device address (cudaGetSymbolAddress) with that device
- * current; make that first call before any stream capture.  All calls share
+ * current; make that first call before any stream capture (a failed lookup
+ * is retried by the next call).  cudaDeviceReset while the library is loaded
+ * is not supported.  All calls share
  * the one array: calls that overlap on the GPU (other streams, other host
  * threads) race on it and must be serialised by the caller.  The array keeps
  * the last call's contents; every call overwrites all of the scratch it reads,

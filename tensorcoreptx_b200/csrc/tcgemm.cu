@@ -777,14 +777,16 @@ namespace {
 static __device__ __align__(256) unsigned char g_s4_static_scratch[TCG_S4_STATIC_SCRATCH_BYTES];
 
 struct StaticScratch {
-    std::once_flag once;
-    cudaError_t err = cudaSuccess;
-    void* ptr = nullptr;
+    std::mutex mu;
+    void* ptr = nullptr;  // set once a lookup has succeeded
 };
 StaticScratch g_s4_static[kMaxDevices];
 
-// Device address of the array on the current device; the lookup runs on the
-// first call per device, with that device current.
+// Device address of the array on the current device.  The lookup runs with
+// that device current, on the first call per device; only a successful
+// lookup is kept, so a call that failed (inside a stream capture, say) is
+// retried by the next one.  cudaDeviceReset is not supported while the
+// library is in use: it unloads the module that holds the array.
 tcg_status static_scratch(void** out)
 {
     int dev = 0;
@@ -792,8 +794,14 @@ tcg_status static_scratch(void** out)
     if (e != cudaSuccess) return cuda_fail(e);
     if (dev < 0 || dev >= kMaxDevices) return TCG_ERR_UNSUPPORTED;
     StaticScratch& s = g_s4_static[dev];
-    std::call_once(s.once, [&]() { s.err = cudaGetSymbolAddress(&s.ptr, g_s4_static_scratch); });
-    if (s.err != cudaSuccess || s.ptr == nullptr) return cuda_fail(s.err != cudaSuccess ? s.err : cudaErrorInvalidSymbol);
+    std::lock_guard<std::mutex> lk(s.mu);
+    if (!s.ptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_s4_static_scratch);
+        if (e != cudaSuccess) return cuda_fail(e);
+        if (!p) return cuda_fail(cudaErrorInvalidSymbol);
+        s.ptr = p;
+    }
     *out = s.ptr;
     return TCG_SUCCESS;
 }

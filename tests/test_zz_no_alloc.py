@@ -12,9 +12,14 @@ This file is named to be collected last, so a `-x` run has finished every
 other test before it.  It calls the entry point through the C ABI (ctypes on
 libtcgemm.so) and checks it, bit for bit, against tcg_gemm_s4 with a
 caller-provided workspace, on two different problems in a row (the second
-smaller, so stale scratch from the first would show).
+smaller, so stale scratch from the first would show), and, in a fresh child
+process, that repeated calls take no device memory.
 """
 import ctypes as C
+import os
+import subprocess
+import sys
+import textwrap
 
 import pytest
 import torch
@@ -82,3 +87,37 @@ def test_static_scratch_rejects_oversize_without_launching():
     torch.cuda.synchronize()
     assert st == TCG_ERR_WORKSPACE
     assert int(C_[0, 0]) == 5 and int(C_[-1, -1]) == 5
+
+
+_CHILD = textwrap.dedent("""
+    import torch
+    from tensorcoreptx_b200 import _native
+    L = _native.lib()
+    torch.cuda.set_device(0)
+    M = N = K = 4096
+    need = L.tcg_gemm_s4_workspace_size(M, N, K, 1)
+    g = torch.Generator(device="cuda:0").manual_seed(7)
+    A = torch.randint(-128, 128, (M, K // 2), generator=g, device="cuda:0", dtype=torch.int8)
+    B = torch.randint(-128, 128, (N, K // 2), generator=g, device="cuda:0", dtype=torch.int8)
+    C = torch.empty(M, N, dtype=torch.int32, device="cuda:0")
+    s = torch.cuda.current_stream().cuda_stream
+    # the first call loads the kernels (lazy module loading takes device
+    # memory for code) and looks up the array's address
+    assert L.tcg_gemm_s4_static(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, 1, s) == 0
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        assert L.tcg_gemm_s4_static(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, 1, s) == 0
+    torch.cuda.synchronize()
+    free1 = torch.cuda.mem_get_info()[0]
+    # any device allocation of the scratch would take `need` bytes (32 MiB)
+    assert free0 - free1 < need, (free0, free1, need)
+    print("NOALLOC_OK", free0 - free1)
+""")
+
+
+def test_static_scratch_takes_no_device_memory_in_a_fresh_process():
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", _CHILD], cwd=root, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0 and "NOALLOC_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
