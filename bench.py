@@ -6,20 +6,37 @@
 Workload: the sharded int8 GEMM, M = N = K = 32768 in total, int8 uniform
 [-128, 127] from a seed, int32 accumulation and output.  A is row-partitioned
 across the ranks (M/G rows each), B is replicated, each rank computes its
-M/G x N slice of C (no data-path collective; ``--gather`` adds the optional
-all-gather of C).  The total problem is fixed, so scaling is "strong"; at one
-GPU this is the full 32768^3 problem on one B200.
+M/G x N slice of C (no data-path collective in the headline step).  The total
+problem is fixed, so scaling is "strong"; at one GPU this is the full 32768^3
+problem on one B200.
+
+Inputs: row block b (256 rows) of A and of BT (N x K) is drawn with
+torch.randint(-128, 128) from a CPU generator seeded from (matrix, b), so
+every rank, and the reference arm, reproduce exactly the rows they need.
 
 A "step" is one GEMM of each rank's slice.  ``value`` is whole-job TOPS with
-inputs resident in HBM (inputs are 2 GiB, larger than L2, so no flush is
+inputs resident in HBM (2 GiB of operands, larger than L2, so no flush is
 needed); ``e2e`` is the same metric through the public host-buffer API
-(``gemm_int8_host``) with the step's A slice and B copied from pinned host
-memory and its C slice copied back inside the timed region.  Device time is measured with CUDA events on
-the launching stream, max over ranks.
+(``gemm_int8_host``): the step's A slice and B come from pinned host memory
+(with more than one GPU each rank copies 1/G of B and the ranks all-gather it
+over NVLink) and the C slice goes back, all inside the timed region.  Device
+time is measured with CUDA events on the launching stream, max over ranks.
+
+After the timed regions (never inside them) the run checks what it timed:
+every rank's whole C slice by Freivalds' check and four rows recomputed in
+float64 on the GPU, the end-to-end C against the resident C, and, at one GPU,
+the rows of the CPU-baseline sample against the reference's own
+cpu_gemm_int8 -- the ``parity`` object of the line.  At one GPU the line also
+carries the reported baselines: the reference's cpu_gemm_int8 and a blocked
+multi-threaded CPU GEMM on the host cores, and the reference's GPU kernels
+recompiled for sm_100a, each timed on this box.  With more than one GPU the
+gathered steps (C all-gathered by the GEMM epilogue's NVLink stores, and by
+NCCL) are timed and checked as extras.
 
 ``--impl reference`` times the reference's own CPU GEMM (src/data_int8.cu
 cpu_gemm_int8, compiled unchanged into oracle/_ref/) on a bounded row sample
-of the same workload with all host threads; only rank 0 runs it.
+of the same workload and the same inputs with all host threads; only rank 0
+runs it.
 """
 from __future__ import annotations
 
@@ -31,12 +48,15 @@ import subprocess
 import sys
 import threading
 import time
+from concurrent.futures import ThreadPoolExecutor
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "GEMM TFLOPS(fp16)/TOPS(int8,int4) per B200 + % dense tensor peak; 8-GPU agg"
 SIZE = 32768
+SEED_A, SEED_B = 1234, 999
+BLOCK_ROWS = 256
 
 
 def parse_args():
@@ -47,8 +67,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--size", type=int, default=SIZE, help="M = N = K of the whole problem")
     ap.add_argument("--gather", choices=["none", "nccl", "p2p"], default="none",
-                    help="all-gather C each step: NCCL after the GEMM, or peer stores from the "
-                         "GEMM epilogue (p2p)")
+                    help="all-gather C in the headline step: NCCL after the GEMM, or peer stores from "
+                         "the GEMM epilogue (p2p); the gathered steps are also timed as extras at N > 1")
     ap.add_argument("--no-extras", action="store_true", help="skip the per-config extras")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0,
@@ -71,6 +91,42 @@ def load_peaks():
         return p, "measured"
     except (OSError, ValueError):
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def workload_config(size, world, gather="none"):
+    """The `config` object both arms print (identical for the same run)."""
+    return {
+        "workload": f"int8 GEMM M=N=K={size}, A row-sharded over {world} GPU(s), B replicated, int32 C"
+                    + {"none": "", "nccl": ", C all-gathered (NCCL, block-cyclic rows, 4 blocks each "
+                                           "gathered while the next multiplies)",
+                       "p2p": ", C all-gathered by the GEMM epilogue over NVLink peer stores"}[gather],
+        "per_rank": f"{size // world}x{size}x{size}",
+        "values": f"int8 uniform [-128,127]; row block b of A / BT from torch CPU generator seed "
+                  f"{SEED_A}*1000003+b / {SEED_B}*1000003+b",
+        "l2": "inputs (2 GiB) larger than L2; no flush",
+        "parallelism": f"rows{world}",
+    }
+
+
+def gen_rows(seed, r0, r1, cols, threads, out=None):
+    """Rows [r0, r1) of the seeded int8 matrix with `cols` columns (a CPU
+    tensor).  Row block b is torch.randint(-128, 128) from a CPU generator
+    seeded seed * 1000003 + b, so any rows can be reproduced alone."""
+    import torch
+    n = r1 - r0
+    if out is None:
+        out = torch.empty((n, cols), dtype=torch.int8)
+    b0, b1 = r0 // BLOCK_ROWS, (r1 + BLOCK_ROWS - 1) // BLOCK_ROWS
+
+    def one(b):
+        g = torch.Generator().manual_seed(seed * 1000003 + b)
+        blk = torch.randint(-128, 128, (BLOCK_ROWS, cols), generator=g, dtype=torch.int8)
+        lo, hi = max(r0, b * BLOCK_ROWS), min(r1, (b + 1) * BLOCK_ROWS)
+        out[lo - r0:hi - r0] = blk[lo - b * BLOCK_ROWS:hi - b * BLOCK_ROWS]
+
+    with ThreadPoolExecutor(max(1, threads)) as ex:
+        list(ex.map(one, range(b0, b1)))
+    return out
 
 
 # ---------------------------------------------------------------- clocks ----
@@ -142,76 +198,89 @@ class ClockSampler:
                 "power_w_max": max(pw) if pw else None, "samples": len(rows), "window": window}
 
 
-# -------------------------------------------------------- reference (CPU) ----
-
-_CPU_INPUTS = {}
 
 
-def _cpu_inputs(size, rows):
-    """Seeded int8 operands for the CPU sample: `rows` rows of A and all of
-    BT (N x K), generated once per process."""
-    import numpy as np
-    if _CPU_INPUTS.get("size") != size:
-        _CPU_INPUTS.clear()
-        _CPU_INPUTS["size"] = size
-        _CPU_INPUTS["BT"] = np.random.default_rng(1).integers(-128, 128, (size, size), dtype=np.int8)
-    if _CPU_INPUTS.get("rows") != rows:
-        _CPU_INPUTS["rows"] = rows
-        _CPU_INPUTS["A"] = np.random.default_rng(0).integers(-128, 128, (rows, size), dtype=np.int8)
-    return _CPU_INPUTS["A"], _CPU_INPUTS["BT"]
+# -------------------------------------------- reference CPU GEMM (sample) ----
+
+def sample_rows(total, n):
+    """The CPU sample's rows of a `total`-row slice: the first n/2 and the last
+    n - n/2 rows (the slice's edges, where a shard or tile boundary error
+    would show)."""
+    n = max(2, min(n, total))
+    first = n // 2
+    return list(range(first)) + list(range(total - (n - first), total))
 
 
-def cpu_reference_sample(size, rows, threads):
-    """Run the reference's own cpu_gemm_int8 (oracle/_ref) -- or, when the
+def cpu_reference_rows(A_rows, BT, threads):
+    """The reference's own cpu_gemm_int8 (oracle/_ref) -- or, when the
     reference was not available at build time, the oracle's restatement --
-    on `rows` rows of C for the size^3 int8 problem.  Returns (seconds, kind)."""
+    on the given rows of A (numpy int8, contiguous) against all of BT.
+    Returns (C rows, seconds, kind)."""
     import numpy as np
     from oracle import oracle as O
 
-    A, BT = _cpu_inputs(size, rows)
-    Cs = np.zeros((rows, size), np.int32)
+    rows, K = A_rows.shape
+    N = BT.shape[0]
+    Cs = np.zeros((rows, N), np.int32)
     t0 = time.perf_counter()
     if O.ref_data_lib("int8") is not None:
-        O.ref_gemm_rows("int8", A, BT, rows, size, size, Cs, 0, rows, threads=threads)
+        O.ref_gemm_rows("int8", A_rows, BT, rows, N, K, Cs, 0, rows, threads=threads)
         kind = "reference"
     else:
-        Cs[:] = O.gemm_s8(A, BT, threads=threads)
+        Cs[:] = O.gemm_s8(A_rows, BT, threads=threads)
         kind = "port"
-    return time.perf_counter() - t0, kind
+    return Cs, time.perf_counter() - t0, kind
 
 
-def cpu_sample_rows(size, threads, target_s):
-    """Rows per sample so one sample takes about target_s seconds."""
-    t, _ = cpu_reference_sample(size, threads, threads)  # one row per thread
-    per_round = max(t, 1e-3)
-    rounds = max(1, int(target_s / per_round))
+def cpu_sample_count(A_rows_fn, BT, threads, target_s):
+    """Rows per sample so one sample takes about target_s seconds (calibrated
+    on one row per thread)."""
+    _, t, _ = cpu_reference_rows(A_rows_fn(sample_rows(threads * 64, threads)), BT, threads)
+    rounds = max(1, int(target_s / max(t, 1e-3)))
     return threads * rounds
 
 
 def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return 0
+    import numpy as np
     size = args.size
     threads = host_threads()
-    rows = cpu_sample_rows(size, threads, min(args.cpu_seconds, 4.0))
+    BT = gen_rows(SEED_B, 0, size, size, threads).numpy()
+
+    def a_rows(idx):
+        # whole 256-row blocks of the global A, generated once each
+        out = np.empty((len(idx), size), np.int8)
+        blocks = {}
+        for j, r in enumerate(idx):
+            b = r // BLOCK_ROWS
+            if b not in blocks:
+                blocks[b] = gen_rows(SEED_A, b * BLOCK_ROWS, min(size, (b + 1) * BLOCK_ROWS), size, 1).numpy()
+            out[j] = blocks[b][r - b * BLOCK_ROWS]
+        return out
+
+    n = cpu_sample_count(a_rows, BT, threads, min(args.cpu_seconds, 4.0))
+    A_s = a_rows(sample_rows(size, n))
+    n = A_s.shape[0]
     times = []
     kind = "reference"
     for i in range(args.warmup + args.steps):
-        t, kind = cpu_reference_sample(size, rows, threads)
+        _, t, kind = cpu_reference_rows(A_s, BT, threads)
         if i >= args.warmup:
             times.append(t)
-    ops = 2.0 * rows * size * size
+    ops = 2.0 * n * size * size
     mean_t = sum(times) / len(times)
     tops = ops / mean_t / 1e12
-    sample = f"{rows} of {size} rows of C per step ({rows}x{size}x{size} int8 MACs), {threads} threads"
+    sample = (f"{n} of {size} rows of C per step (the first {n // 2} and last {n - n // 2}; "
+              f"{n}x{size}x{size} int8 MACs), {threads} threads")
     line = {
-        "metric": METRIC, "value": tops, "unit": "TOPS", "n_gpus": args.gpus, "steps": args.steps,
+        "metric": METRIC, "value": tops, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": mean_t * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": f"int8 GEMM M=N=K={size}, A row-sharded, B replicated, int32 C",
-                   "parallelism": f"rows{args.gpus}"},
+        "config": workload_config(size, world),
         "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": tops, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
@@ -221,6 +290,73 @@ def run_reference_arm(args):
 
 
 # ------------------------------------------------------------- our arm ----
+
+def timed(stream, fn, steps, warmup, barrier):
+    """Run fn warmup times, then `steps` times between events on `stream`
+    (barrier + synchronize on both sides).  Returns (total ms, per-step ms)."""
+    import torch
+    for _ in range(max(warmup, 3)):
+        fn()
+    stream.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for i in range(steps):
+        ev[i][0].record(stream)
+        fn()
+        ev[i][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    return t0.elapsed_time(t1), [a.elapsed_time(b) for a, b in ev]
+
+
+def gathered_legs(args, A, BT, r0, rows, size, world, dev, stream, barrier, max_over_ranks):
+    """The optional all-gather of C (more than one GPU): the GEMM epilogue
+    storing every tile into all ranks' C over NVLink (p2p), and block-cyclic
+    row blocks all-gathered by NCCL while the next block multiplies (nccl).
+    Each is timed like the headline step and its full gathered C checked by
+    Freivalds' check against the full A."""
+    import torch
+    import torch.distributed as dist
+
+    from tensorcoreptx_b200.dist import PeerGather, cyclic_row_blocks, gathered_gemm_int8
+    from tensorcoreptx_b200.verify import freivalds_int8
+
+    out = {}
+    A_full = torch.empty((size, size), dtype=torch.int8, device=dev)
+    dist.all_gather_into_tensor(A_full, A)
+    sent = rows * size * 4 * (world - 1)
+    ops = 2.0 * size ** 3
+    peer = PeerGather(size, size, dev)
+    with torch.cuda.stream(stream):
+        total, _ = timed(stream, lambda: peer.gemm_int8(A, BT, r0), args.steps, args.warmup, barrier)
+    ms = max_over_ranks(total) / args.steps
+    ok = freivalds_int8(A_full, BT, peer.C)
+    bad = max_over_ranks(0.0 if ok else 1.0)
+    out["gather_p2p"] = {"ms_per_step": ms, "tops": ops / ms / 1e9, "nvlink_bytes_sent_per_rank": sent,
+                         "nvlink_bound_ms": sent / 770e9 * 1e3, "freivalds_pass": bad == 0.0}
+    peer.close()
+    del peer
+    torch.cuda.empty_cache()
+    chunks = 4
+    A_cyc = torch.cat([A_full[b0:b1] for b0, b1 in cyclic_row_blocks(size, world, dist.get_rank(), chunks)])
+    C_full = torch.empty((size, size), dtype=torch.int32, device=dev)
+    with torch.cuda.stream(stream):
+        total, _ = timed(stream, lambda: gathered_gemm_int8(A_cyc, BT, chunks, out=C_full), args.steps,
+                         args.warmup, barrier)
+    ms = max_over_ranks(total) / args.steps
+    ok = freivalds_int8(A_full, BT, C_full)
+    bad = max_over_ranks(0.0 if ok else 1.0)
+    out["gather_nccl"] = {"ms_per_step": ms, "tops": ops / ms / 1e9, "nvlink_bytes_sent_per_rank": sent,
+                          "nvlink_bound_ms": sent / 770e9 * 1e3, "freivalds_pass": bad == 0.0}
+    del A_full, A_cyc, C_full
+    torch.cuda.empty_cache()
+    return out
+
 
 def run_ours(args):
     import torch
@@ -239,13 +375,14 @@ def run_ours(args):
 
     from tensorcoreptx_b200.dist import max_over_ranks as _max_over_ranks
     from tensorcoreptx_b200.dist import shard_rows
+    from tensorcoreptx_b200.verify import freivalds_int8, rows_int8
 
     size = args.size
     r0, r1 = shard_rows(size, world, rank, align=256)
     rows = r1 - r0
     gather = args.gather if world > 1 else "none"
-    if gather != "none" and size % world != 0:
-        raise SystemExit("--gather needs the rows to divide evenly across ranks")
+    if (gather != "none" or (world > 1 and not args.no_extras)) and size % (world * 4 * 256):
+        raise SystemExit("the gathered steps need the rows to split into 4 equal 256-row blocks per rank")
     ops_total = 2.0 * size * size * size
     ops_rank = 2.0 * rows * size * size
 
@@ -256,13 +393,13 @@ def run_ours(args):
     def max_over_ranks(x: float) -> float:
         return _max_over_ranks(x, device=dev)
 
-    # inputs: A slice of this rank, full B (BT layout, N x K), seeded on the GPU
-    g = torch.Generator(device=dev).manual_seed(1234)
-    A_full_seed_offset = rank  # each rank draws its own rows of the global A
-    g.manual_seed(1234 + A_full_seed_offset)
-    A = torch.randint(-128, 128, (rows, size), generator=g, device=dev, dtype=torch.int8)
-    g.manual_seed(999)  # identical B on every rank (replicated)
-    BT = torch.randint(-128, 128, (size, size), generator=g, device=dev, dtype=torch.int8)
+    # inputs: this rank's rows of A and all of BT (N x K), generated on the
+    # host, kept pinned for the end-to-end leg and copied to the device once
+    threads = max(1, host_threads() // world)
+    A_h = gen_rows(SEED_A, r0, r1, size, threads).pin_memory()
+    B_h = gen_rows(SEED_B, 0, size, size, threads).pin_memory()
+    A = A_h.to(dev)
+    BT = B_h.to(dev)
     C = torch.empty(rows, size, dtype=torch.int32, device=dev)
     C_full = torch.empty(size, size, dtype=torch.int32, device=dev) if gather == "nccl" else None
     peer = None
@@ -273,8 +410,20 @@ def run_ours(args):
     from tensorcoreptx_b200 import _native as nat
     lib = nat.lib()
     stream = torch.cuda.Stream(device=dev)
+    nccl_chunks = 4
+    A_step = A
+    if gather == "nccl":
+        from tensorcoreptx_b200.dist import cyclic_row_blocks, gathered_gemm_int8
+        A_all = torch.empty((size, size), dtype=torch.int8, device=dev)
+        dist.all_gather_into_tensor(A_all, A)
+        A_step = torch.cat([A_all[b0:b1] for b0, b1 in cyclic_row_blocks(size, world, rank, nccl_chunks)])
+        del A_all
 
-    def gemm_launch():
+    def step():
+        if gather == "nccl":
+            with torch.cuda.stream(stream):
+                gathered_gemm_int8(A_step, BT, nccl_chunks, out=C_full)
+            return
         if peer is not None:
             with torch.cuda.stream(stream):
                 peer.gemm_int8(A, BT, r0)  # GEMM + epilogue stores to every rank + 1-word barrier
@@ -283,31 +432,17 @@ def run_ours(args):
                              nat.TCG_B_NK, stream.cuda_stream)
         nat.check("tcg_gemm_s8", st)
 
-    # --gather nccl: block-cyclic row blocks, each multiplied into its place
-    # in the full C and all-gathered in place while the next one multiplies
-    nccl_chunks = 4
-    if gather == "nccl" and rows % nccl_chunks:
-        raise SystemExit("--gather nccl needs each rank's rows to split into 4 blocks")
-
-    def step():
-        if gather == "nccl":
-            from tensorcoreptx_b200.dist import gathered_gemm_int8
-            with torch.cuda.stream(stream):
-                gathered_gemm_int8(A, BT, nccl_chunks, out=C_full)
-            return
-        gemm_launch()
-
     clocks = ClockSampler(list(range(world)) if rank == 0 else [local])
     if rank == 0:
         clocks.start()
         time.sleep(0.5)
 
+    # ---- kernel-resident timed region
+    clocks.mark("warmup")
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):
             step()
     stream.synchronize()
-
-    # ---- kernel-resident timed region
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
     barrier()
@@ -333,20 +468,59 @@ def run_ours(args):
     werr = T.check_device_error(stream)
     assert werr == 0
 
+    # ---- parity of what was timed (outside the timed region)
+    if gather == "nccl":
+        C_mine = C_full
+        A_chk = torch.empty((size, size), dtype=torch.int8, device=dev)
+        dist.all_gather_into_tensor(A_chk, A)
+    elif gather == "p2p":
+        C_mine, A_chk = peer.C, None
+        A_chk = torch.empty((size, size), dtype=torch.int8, device=dev)
+        dist.all_gather_into_tensor(A_chk, A)
+    else:
+        C_mine, A_chk = C, A
+    fv_ok = freivalds_int8(A_chk, BT, C_mine, trials=2, seed=rank)
+    chk_rows = sorted({0, 1, C_mine.shape[0] - 2, C_mine.shape[0] - 1})
+    rows_ok = bool(torch.equal(rows_int8(A_chk, BT, chk_rows), C_mine[chk_rows]))
+    del A_chk
+    if gather != "none":  # the e2e leg and the reference rows compare against the plain slice
+        with torch.cuda.stream(stream):
+            nat.check("tcg_gemm_s8", lib.tcg_gemm_s8(A.data_ptr(), BT.data_ptr(), C.data_ptr(), rows, size,
+                                                     size, 1, nat.TCG_B_NK, stream.cuda_stream))
+        stream.synchronize()
     if peer is not None:
         peer.close()
         del peer
+    C_full = None
+    torch.cuda.empty_cache()
+
+    # ---- clock-normalised kernel rate: time x median SM clock, TOPS per GHz
+    ksum = clocks.summary("kernel")
+    mhz = ksum.get("sm_mhz")
+    achieved = ops_rank / (kern_ms * 1e-3) / 1e12
+    clock_norm = None
+    if mhz:
+        clock_norm = {"sm_mhz_median": mhz, "kernel_ms_x_ghz": kern_ms * mhz / 1e3,
+                      "tops_per_ghz_per_gpu": achieved / (mhz / 1e3),
+                      "note": "per-GPU kernel TOPS divided by the median SM clock of the timed window; "
+                              "comparable across N with the power cap removed"}
+
+    # ---- the gathered steps (N > 1), timed and checked as extras
+    gathered = None
+    if world > 1 and not args.no_extras:
+        gathered = gathered_legs(args, A, BT, r0, rows, size, world, dev, stream, barrier, max_over_ranks)
+
     # ---- end-to-end through the public API: pinned host in, pinned host out
-    A_h = A.cpu().pin_memory()
-    B_h = BT.cpu().pin_memory()
     C_h = torch.empty(rows, size, dtype=torch.int32).pin_memory()
-    del A, BT, C
+    group = dist.group.WORLD if world > 1 else None
+    del A, BT
     torch.cuda.empty_cache()
 
     def e2e_step():
-        # public host-buffer entry: pinned A slice and B in, pinned C slice out,
-        # row chunks of C pipelined against the copies
-        T.gemm_int8_host(A_h, B_h, out=C_h, chunks=8)
+        # public host-buffer entry: pinned A slice and B in (1/G of B per rank
+        # plus an NVLink all-gather when G > 1), pinned C slice out, row x
+        # column blocks of C pipelined against the copies
+        T.gemm_int8_host(A_h, B_h, out=C_h, chunks=8, group=group)
 
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):
@@ -367,13 +541,22 @@ def run_ours(args):
     barrier()
     clocks.mark(None)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
-    h2d = rows * size + size * size
+    h2d = rows * size + (size * size // world if world > 1 else size * size)
     d2h = rows * size * 4
-    del A_h, B_h, C_h
+    e2e_ok = bool(torch.equal(C_h.to(dev), C))
+    del C
     torch.cuda.empty_cache()
 
     if rank == 0:
         clocks.stop()
+    bad = max_over_ranks(0.0 if (fv_ok and rows_ok and e2e_ok) else 1.0)
+    parity = {"freivalds_trials": 2, "freivalds_pass": fv_ok, "rows_fp64_device": len(chk_rows),
+              "rows_fp64_device_pass": rows_ok, "e2e_equals_resident": e2e_ok,
+              "all_ranks_pass": bad == 0.0,
+              "what": "every rank: its whole C slice by Freivalds' check (C x == A (B^T x), exact in "
+                      "float64), rows 0, 1, last-1, last recomputed in float64 on the GPU, and the "
+                      "end-to-end C equal to the resident C"}
+    parity["pass"] = parity["all_ranks_pass"]
 
     result = None
     if rank == 0:
@@ -382,7 +565,6 @@ def run_ours(args):
         # 2.25 PFLOP/s nominal).  The kernel is timed alone, back to back, so
         # the burst bf16 figure is the denominator.
         peak_tops = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
-        achieved = ops_rank / (kern_ms * 1e-3) / 1e12
         traffic = profile_traffic(size, rows)
         ms_per_step = total_ms / args.steps
         result = {
@@ -398,20 +580,8 @@ def run_ours(args):
             "vs_baseline": None,
             "dtype": "int8",
             "data": "synthetic",
-            "config": {
-                "workload": f"int8 GEMM M=N=K={size}, A row-sharded over {world} GPU(s), "
-                            f"B replicated, int32 C" + {"none": "", "nccl": ", C all-gathered (NCCL, block-cyclic rows, "
-                                                                 "4 blocks each gathered while the next "
-                                                                 "multiplies)",
-                                                         "p2p": ", C all-gathered by the GEMM epilogue "
-                                                                "over NVLink peer stores"}[gather],
-                "per_rank": f"{rows}x{size}x{size}",
-                "values": "int8 uniform [-128,127], seeded",
-                "l2": "inputs (2 GiB) larger than L2; no flush",
-                "tile_m": tile_m,
-                "tile_n": tile_n,
-                "parallelism": f"rows{world}",
-            },
+            "config": workload_config(size, world, gather),
+            "tile": {"m": tile_m, "n": tile_n},
             "roofline": {
                 "bound": "tensor",
                 "achieved": achieved,
@@ -425,14 +595,18 @@ def run_ours(args):
             "e2e": {"value": ops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": args.steps * (nccl_chunks if gather == "nccl" else 1),
-            "clocks": clocks.summary("kernel"),
+            "clocks": ksum,
+            "clock_norm": clock_norm,
             "clocks_e2e": clocks.summary("e2e"),
+            "parity": parity,
         }
+        if gathered is not None:
+            result["extras"] = gathered
 
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-    return result
+    return result, (A_h, B_h, C_h)
 
 
 def profile_traffic(size, rows):
@@ -455,6 +629,26 @@ def profile_traffic(size, rows):
 
 # ----------------------------------------------------------- extras (N=1) ----
 
+def time_fn(fn, iters, pause=0.5):
+    """Mean ms per call on the current stream after 3 warm-ups.  Every
+    configuration starts from an idle GPU: without the pause, one timed right
+    after a long power-capped loop inherits its clocks."""
+    import torch
+    torch.cuda.synchronize()
+    time.sleep(pause)
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
 def extras():
     """Kernel-only throughput of the other benchmark configurations on this
     GPU, for context (one-GPU runs only)."""
@@ -464,24 +658,6 @@ def extras():
 
     dev = torch.device("cuda", 0)
     out = {}
-
-    def time_fn(fn, iters):
-        # every configuration starts from an idle GPU: without the pause, one
-        # timed right after a long power-capped loop inherits its clocks
-        torch.cuda.synchronize()
-        time.sleep(0.5)
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize()
-        s = torch.cuda.Event(enable_timing=True)
-        e = torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(iters):
-            fn()
-        e.record()
-        torch.cuda.synchronize()
-        return s.elapsed_time(e) / iters
-
     g = torch.Generator(device=dev).manual_seed(0)
     n = 4096
     A = torch.randint(-128, 128, (n, n), generator=g, device=dev, dtype=torch.int8)
@@ -500,10 +676,9 @@ def extras():
     del B_kn
     Ap = torch.randint(-128, 128, (n, n // 2), generator=g, device=dev, dtype=torch.int8)
     Bp = torch.randint(-128, 128, (n, n // 2), generator=g, device=dev, dtype=torch.int8)
-    ws = torch.empty(T.int4_workspace_size(n, n, n), dtype=torch.uint8, device=dev)
-    ms = time_fn(lambda: T.gemm_int4(Ap, Bp, workspace=ws), 50)
+    ms = time_fn(lambda: T.gemm_int4(Ap, Bp), 50)
     out["int4_4096"] = {"tops": 2 * n ** 3 / ms / 1e9, "ms": ms}
-    del A, BT, Ap, Bp, ws
+    del A, BT, Ap, Bp
     # smallest sizes first and both accumulation modes per size: a size timed
     # right after a power-capped 16384^3 loop would run at reduced clocks
     for n in (512, 1024, 2048, 4096, 8192, 16384):
@@ -587,14 +762,103 @@ def extras():
     return out
 
 
-def cpu_baseline_line(args):
+# --------------------------------------------- reported baselines (N=1) ----
+#
+# Everything below runs after the timed regions and only reports: the
+# reference's own code (its CPU GEMM and its GPU kernels, compiled unchanged
+# into oracle/_ref/) and a blocked CPU GEMM, each on this box.
+
+def cpu_baseline_leg(args, A_h, B_h, C_h):
+    """The reference's cpu_gemm_int8 on a row sample of this run's own inputs
+    (all host threads), timed -- and its rows compared with the GPU's C rows
+    of the same inputs (the row-level parity of the headline config)."""
+    import numpy as np
     size = args.size
     threads = host_threads()
-    rows = cpu_sample_rows(size, threads, args.cpu_seconds)
-    t, kind = cpu_reference_sample(size, rows, threads)
-    return {"value": 2.0 * rows * size * size / t / 1e12, "unit": "TOPS", "cores": threads,
-            "kind": kind,
-            "sample": f"{rows} of {size} rows of C ({rows}x{size}x{size} int8 MACs) in {t:.1f} s"}
+    A_np = A_h.numpy()
+    B_np = B_h.numpy()
+
+    def a_rows(idx):
+        return np.ascontiguousarray(A_np[idx])
+
+    n = cpu_sample_count(a_rows, B_np, threads, args.cpu_seconds)
+    idx = sample_rows(A_np.shape[0], n)
+    ref, t, kind = cpu_reference_rows(a_rows(idx), B_np, threads)
+    n = len(idx)
+    ok = bool(np.array_equal(ref, C_h.numpy()[idx]))
+    line = {"value": 2.0 * n * size * size / t / 1e12, "unit": "TOPS", "cores": threads, "kind": kind,
+            "sample": f"{n} of {size} rows of C (the first {n // 2} and last {n - n // 2} of this run's own "
+                      f"inputs; {n}x{size}x{size} int8 MACs) in {t:.1f} s"}
+    return line, {"rows_vs_reference_cpu": n, "rows_vs_reference_cpu_pass": ok,
+                  "reference_cpu_kind": kind}
+
+
+def blocked_cpu_leg():
+    """The blocked multi-threaded CPU GEMM (oracle/cpu_blocked.c) on all host
+    threads: fp16 512^3, int8 4096^3, int4 4096^3 (best of 3)."""
+    import numpy as np
+    from oracle import oracle as O
+    threads = host_threads()
+    rng = np.random.default_rng(0)
+    out = {"cores": threads, "what": "cache-blocked AVX2 CPU GEMM, all host threads, best of 3"}
+
+    def best(fn):
+        fn()
+        ts = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return min(ts)
+
+    n = 512
+    Ah = rng.uniform(-1, 1, (n, n)).astype(np.float16).view(np.uint16)
+    Bh = rng.uniform(-1, 1, (n, n)).astype(np.float16).view(np.uint16)
+    t = best(lambda: O.blocked_gemm_f16(Ah, Bh, threads=threads))
+    out["fp16_512"] = {"tflops": 2 * n ** 3 / t / 1e12, "ms": t * 1e3}
+    n = 4096
+    A8 = rng.integers(-128, 128, (n, n), dtype=np.int8)
+    B8 = rng.integers(-128, 128, (n, n), dtype=np.int8)
+    t = best(lambda: O.blocked_gemm_s8(A8, B8, threads=threads))
+    out["int8_4096"] = {"tops": 2 * n ** 3 / t / 1e12, "ms": t * 1e3}
+    A4 = rng.integers(-128, 128, (n, n // 2), dtype=np.int8)
+    B4 = rng.integers(-128, 128, (n, n // 2), dtype=np.int8)
+    t = best(lambda: O.blocked_gemm_s4(A4, B4, n, threads=threads))
+    out["int4_4096"] = {"tops": 2 * n ** 3 / t / 1e12, "ms": t * 1e3}
+    return out
+
+
+def reference_kernels_leg():
+    """The reference's GPU kernels recompiled unchanged for sm_100a
+    (oracle/_ref/libref_<kernel>.so), timed on this B200 like ours: int8 and
+    int4 at 4096^3, fp16 at 512^3 and 4096^3."""
+    import torch
+    from oracle import ref_kernels as RK
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    out = {}
+    n = 4096
+    A = torch.randint(-128, 128, (n, n), generator=g, device=dev, dtype=torch.int8)
+    B = torch.randint(-128, 128, (n, n), generator=g, device=dev, dtype=torch.int8)
+    for name in ("int8_wmma", "int8_ptx_mma_k32"):
+        if RK.available(name):
+            ms = time_fn(lambda: RK.run(name, A, B, n, n, n), 10)
+            out[f"{name}_4096"] = {"tops": 2 * n ** 3 / ms / 1e9, "ms": ms}
+    Ap, Bp = A[:, :n // 2].contiguous(), B[:, :n // 2].contiguous()
+    for name in ("int4_wmma", "int4_ptx_mma_k64_x4_x2nontrans_ca"):
+        if RK.available(name):
+            ms = time_fn(lambda: RK.run(name, Ap, Bp, n, n, n), 10)
+            out[f"{name}_4096"] = {"tops": 2 * n ** 3 / ms / 1e9, "ms": ms}
+    del A, B, Ap, Bp
+    for n in (512, 4096):
+        Ah = (torch.rand(n, n, generator=g, device=dev) * 2 - 1).half()
+        Bh = (torch.rand(n, n, generator=g, device=dev) * 2 - 1).half()
+        for name in ("fp16_wmma", "fp16_ptx_fp16acc"):
+            if RK.available(name):
+                ms = time_fn(lambda: RK.run(name, Ah, Bh, n, n, n), 10 if n > 512 else 50)
+                out[f"{name}_{n}"] = {"tflops": 2 * n ** 3 / ms / 1e9, "ms": ms}
+    torch.cuda.empty_cache()
+    return out
 
 
 def main():
@@ -606,14 +870,22 @@ def main():
     sys.stdout.flush()
     json_fd = os.dup(1)
     os.dup2(2, 1)
-    result = run_ours(args)
+    result, host = run_ours(args)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank == 0 and result is not None:
         if world == 1 and not args.no_cpu_baseline:
-            result["cpu_baseline"] = cpu_baseline_line(args)
+            line, rows = cpu_baseline_leg(args, *host)
+            result["cpu_baseline"] = line
+            result["parity"].update(rows)
+            result["parity"]["pass"] = result["parity"]["pass"] and rows["rows_vs_reference_cpu_pass"]
+        del host
         if world == 1 and not args.no_extras:
-            result["extras"] = extras()
+            ex = extras()
+            ex["reference_kernels_b200"] = reference_kernels_leg()
+            if not args.no_cpu_baseline:
+                ex["cpu_blocked"] = blocked_cpu_leg()
+            result["extras"] = ex
         sys.stdout.flush()
         os.write(json_fd, (json.dumps(result) + "\n").encode())
     return 0

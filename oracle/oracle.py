@@ -9,6 +9,9 @@ It wraps two shared libraries:
 * ``oracle/liboracle.so`` -- the plain-C restatement of the reference's host
   code (``oracle/tcg_oracle.c``; every function cites the reference
   ``src/data*.cu`` lines it follows);
+* ``oracle/libcpu_blocked.so`` -- a cache-blocked, multi-threaded CPU GEMM
+  (``oracle/cpu_blocked.c``): the host-core baseline reported beside the GPU
+  numbers, exact for integers like the reference's naive loops;
 * ``oracle/_ref/libref_data_*.so`` -- the reference's own ``src/data.cu``,
   ``src/data_int8.cu`` and ``src/data_int4.cu`` compiled unchanged from source
   (``make -C oracle ref``).  They pin the restatement and serve as the
@@ -103,6 +106,63 @@ def lib():
 def _ptr(a: np.ndarray):
     assert a.flags["C_CONTIGUOUS"]
     return a.ctypes.data_as(C.c_void_p)
+
+
+_blocked = None
+
+
+def blocked_lib():
+    """oracle/libcpu_blocked.so (built on first use like liboracle.so)."""
+    global _blocked
+    with _lock:
+        if _blocked is None:
+            path = os.path.join(HERE, "libcpu_blocked.so")
+            if not os.path.exists(path):
+                import subprocess
+                subprocess.check_call(["make", "-s", "-C", HERE, "all"])
+            L = C.CDLL(path)
+            L.cpu_blocked_gemm_s8.restype = None
+            L.cpu_blocked_gemm_s8.argtypes = [_p, _p, _p, _i, _i, _i, _i]
+            L.cpu_blocked_gemm_s4.restype = _i
+            L.cpu_blocked_gemm_s4.argtypes = [_p, _p, _p, _i, _i, _i, _i]
+            L.cpu_blocked_gemm_f16.restype = _i
+            L.cpu_blocked_gemm_f16.argtypes = [_p, _p, _p, _i, _i, _i, _i]
+            _blocked = L
+    return _blocked
+
+
+def blocked_gemm_s8(A, BT, threads=1):
+    """C = A x BT^T (int8 -> int32) with the blocked multi-threaded CPU GEMM."""
+    A = np.ascontiguousarray(A, np.int8)
+    BT = np.ascontiguousarray(BT, np.int8)
+    M, K = A.shape
+    N = BT.shape[0]
+    Cm = np.empty((M, N), np.int32)
+    blocked_lib().cpu_blocked_gemm_s8(_ptr(A), _ptr(BT), _ptr(Cm), M, N, K, threads)
+    return Cm
+
+
+def blocked_gemm_s4(Ap, BTp, K, threads=1):
+    """C = A x BT^T for packed int4 operands (K/2 bytes per row)."""
+    Ap = np.ascontiguousarray(Ap, np.int8)
+    BTp = np.ascontiguousarray(BTp, np.int8)
+    M, N = Ap.shape[0], BTp.shape[0]
+    Cm = np.empty((M, N), np.int32)
+    if blocked_lib().cpu_blocked_gemm_s4(_ptr(Ap), _ptr(BTp), _ptr(Cm), M, N, K, threads) != 0:
+        raise MemoryError("cpu_blocked_gemm_s4: scratch allocation failed")
+    return Cm
+
+
+def blocked_gemm_f16(A_bits, B_bits, threads=1):
+    """C (fp32) = A x B for fp16 bit patterns (A M x K, B K x N)."""
+    A_bits = np.ascontiguousarray(A_bits, np.uint16)
+    B_bits = np.ascontiguousarray(B_bits, np.uint16)
+    M, K = A_bits.shape
+    N = B_bits.shape[1]
+    Cm = np.empty((M, N), np.float32)
+    if blocked_lib().cpu_blocked_gemm_f16(_ptr(A_bits), _ptr(B_bits), _ptr(Cm), M, N, K, threads) != 0:
+        raise MemoryError("cpu_blocked_gemm_f16: scratch allocation failed")
+    return Cm
 
 
 # --------------------------------------------------------------------------

@@ -1,7 +1,9 @@
 """Run the reference's own GPU kernels, recompiled unchanged for sm_100a into
 oracle/_ref/libref_<kernel>.so (``make -C oracle ref``), on torch tensors.
 
-Test / baseline infrastructure only.  Each library exposes
+Test / baseline infrastructure only: the GPU tests compare against these
+kernels, and bench.py reports their speed as a baseline (outside its timed
+region).  Each library exposes
 ``int ref_launch(A, B, C, M, N, K, batches, stream)`` around the kernel file's
 ``launch_kernel`` (oracle/ref_kernel_shim.cu).  The reference kernels need
 M % 32 == 0, N % 64 == 0 and K a multiple of their K tile (they do not
@@ -10,8 +12,7 @@ bounds-check), so callers only use such shapes.
 import ctypes as C
 import os
 
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF_DIR = os.path.join(ROOT, "oracle", "_ref")
+REF_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ref")
 
 KERNELS = {
     "fp16_wmma": "fp16", "fp16_ptx_fp16acc": "fp16",

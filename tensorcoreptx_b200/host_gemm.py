@@ -120,11 +120,19 @@ def _c_block_offsets(M, N, blocks):
 
 
 def gemm_int8_host(A: torch.Tensor, BT: torch.Tensor, out: torch.Tensor | None = None,
-                   chunks: int = 8, device=None) -> torch.Tensor:
+                   chunks: int = 8, device=None, group=None) -> torch.Tensor:
     """C[M,N] int32 = A[M,K] int8 x BT[N,K]^T int8, all three in (pinned) host
     memory; the multiply runs on the current CUDA device in chunks x chunks
     blocks overlapped with the copies.  Synchronise the current stream before
-    reading C."""
+    reading C.
+
+    Row-sharded use (one process per GPU, A and C this rank's rows, BT the
+    same on every rank): with ``group`` given (a torch.distributed group of
+    more than one rank), every rank copies only its 1/G share of each column
+    chunk of BT from host memory and the chunk is all-gathered over the group
+    (NCCL; NVLink between the GPUs of one box), so each byte of B crosses PCIe
+    once per step instead of once per rank.  Every rank of the group must make
+    the same call (same N, K and chunks) in the same order."""
     _check_host(A, "A", torch.int8)
     _check_host(BT, "BT", torch.int8)
     _check(A.size(1) == BT.size(1), "A cols must equal BT cols (both = K)")
@@ -133,6 +141,9 @@ def gemm_int8_host(A: torch.Tensor, BT: torch.Tensor, out: torch.Tensor | None =
     C = out if out is not None else torch.empty((M, N), dtype=torch.int32, pin_memory=True)
     _check_host(C, "out", torch.int32)
     _check(tuple(C.shape) == (M, N), "out must be M x N")
+    if group is not None:
+        # the collectives follow the column chunks: every rank must reach them
+        _check(M > 0 and N > 0, "row-sharded use needs rows and columns on every rank")
     if M == 0 or N == 0:
         return C
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
@@ -146,8 +157,23 @@ def gemm_int8_host(A: torch.Tensor, BT: torch.Tensor, out: torch.Tensor | None =
     def copy_a(r0, r1, stream):
         A_d[r0:r1].copy_(A[r0:r1], non_blocking=True)
 
+    world = 1
+    if group is not None:
+        import torch.distributed as dist
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+
     def copy_b(c0, c1, stream):
-        B_d[c0:c1].copy_(BT[c0:c1], non_blocking=True)
+        if world > 1 and (c1 - c0) % world == 0:
+            # this rank's share of the chunk from host memory, the rest from
+            # the other ranks (in-place all-gather on this stream's order)
+            import torch.distributed as dist
+            sh = (c1 - c0) // world
+            mine = B_d[c0 + rank * sh:c0 + (rank + 1) * sh]
+            mine.copy_(BT[c0 + rank * sh:c0 + (rank + 1) * sh], non_blocking=True)
+            dist.all_gather_into_tensor(B_d[c0:c1], mine, group=group)
+        else:
+            B_d[c0:c1].copy_(BT[c0:c1], non_blocking=True)
 
     def launch(r0, r1, c0, c1, stream):
         st = L.tcg_gemm_s8(A_d.data_ptr() + r0 * K, B_d.data_ptr() + c0 * K,

@@ -1,7 +1,8 @@
 """Row-sharded GEMM over NCCL on 2 GPUs (skipped with fewer GPUs): every
 rank's gathered C -- one all-gather after the GEMM, block-cyclic blocks
 gathered while the next multiplies, and the GEMM epilogue's peer stores --
-equals the single-GPU product of the full matrices."""
+equals the single-GPU product of the full matrices; so does the host-buffer
+GEMM of each rank's rows with B copied in halves and all-gathered."""
 import os
 import socket
 
@@ -56,6 +57,14 @@ def _worker(rank, world, port, q):
                 torch.cuda.synchronize()
                 ok = ok and bool(torch.equal(Cp, full))
             dist.barrier()
+        # host-buffer GEMM of this rank's rows with B shared: each rank copies
+        # half of every column chunk of BT from host memory, NCCL gathers it
+        A_h = A[r0:r1].cpu().pin_memory()
+        BT_h = BT.cpu().pin_memory()
+        for chunks in (2, 3):
+            C_h = T.gemm_int8_host(A_h, BT_h, chunks=chunks, group=dist.group.WORLD)
+            torch.cuda.synchronize()
+            ok = ok and bool(torch.equal(C_h, full[r0:r1].cpu()))
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, ok, ""))

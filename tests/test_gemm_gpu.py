@@ -16,7 +16,7 @@ import torch
 
 from oracle import oracle as O
 
-from . import ref_kernels as RK
+from oracle import ref_kernels as RK
 
 pytestmark = pytest.mark.gpu
 
@@ -155,6 +155,30 @@ def test_int8_4096_full_size():
         ref = O.gemm_s8(A, BT, row0=r0, rows=1)
         assert np.array_equal(C[r0], ref[r0])
     assert freivalds_int(At, Bt, Ct, b_kn=False)
+
+
+def test_int8_c_above_2gib():
+    """A C of 3 GiB (24576 x 32768 int32): byte offsets above 2^31, the
+    pair-wide tiles and cluster-launch-control grid of the 32768^3 benchmark
+    class.  Whole product by Freivalds' check, four rows recomputed in
+    float64 on the GPU, the first and last rows against the oracle."""
+    from tensorcoreptx_b200.verify import freivalds_int8, rows_int8
+    M, N, K = 24576, 32768, 4096
+    rng = np.random.default_rng(24576)
+    A = rand_s8(rng, (M, K))
+    BT = rand_s8(rng, (N, K))
+    At, Bt = _cuda(A), _cuda(BT)
+    Ct = tcg().gemm_int8(At, Bt)
+    assert Ct.numel() * 4 > (1 << 31)
+    assert tcg().last_tile_m() == 512
+    assert freivalds_int8(At, Bt, Ct, trials=2)
+    rows = [0, 12345, M - 2, M - 1]
+    assert torch.equal(rows_int8(At, Bt, rows), Ct[rows])
+    for r in (0, M - 1):
+        ref = O.gemm_s8(A[r:r + 1], BT)
+        assert np.array_equal(Ct[r].cpu().numpy(), ref[0])
+    del Ct
+    torch.cuda.empty_cache()
 
 
 # ------------------------------------------------------------------ int4 ----

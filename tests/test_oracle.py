@@ -192,3 +192,28 @@ def test_f8_decoding_matches_torch():
         ref = torch.from_numpy(codes).view(dt).to(torch.float64).numpy()
         same = (mine == ref) | (np.isnan(mine) & np.isnan(ref))
         assert same.all(), (fmt, codes[~same][:5])
+
+
+# ------------------------------------------------- blocked CPU baseline ----
+
+@pytest.mark.parametrize("M,N,K", [(64, 64, 64), (67, 33, 48), (130, 257, 4112), (1, 5, 16), (9, 4, 2050)])
+def test_blocked_cpu_gemm_s8_exact(M, N, K):
+    """The host-core baseline computes the reference's integer product exactly."""
+    rng = np.random.default_rng(M + N + K)
+    A = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    BT = rng.integers(-128, 128, (N, K), dtype=np.int8)
+    assert np.array_equal(O.blocked_gemm_s8(A, BT, threads=3), O.gemm_s8(A, BT))
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 64, 64), (96, 80, 128), (33, 65, 256)])
+def test_blocked_cpu_gemm_s4_exact(M, N, K):
+    Ap, BTp = O.generate_int4_packed(M, N, K)
+    assert np.array_equal(O.blocked_gemm_s4(Ap[0], BTp[0], K, threads=2), O.gemm_s4(Ap[0], BTp[0], K))
+
+
+def test_blocked_cpu_gemm_f16_within_tolerance():
+    rng = np.random.default_rng(3)
+    A = rng.uniform(-1, 1, (70, 300)).astype(np.float16).view(np.uint16)
+    B = rng.uniform(-1, 1, (300, 260)).astype(np.float16).view(np.uint16)
+    err = np.abs(O.blocked_gemm_f16(A, B, threads=4) - O.gemm_f16_f64(A, B)).max()
+    assert err <= O.fp16_tolerance(A, B, 300) * 1e-3

@@ -11,7 +11,7 @@ import torch
 
 from oracle import oracle as O
 
-from . import ref_kernels as RK
+from oracle import ref_kernels as RK
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
