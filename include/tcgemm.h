@@ -93,10 +93,14 @@ tcg_status tcg_gemm_f8(const void* A, const void* B, float* C, int M, int N, int
 /* packed int4 x int4 -> int32, exact; B is always BT (N x K/2 bytes).
  * Replaces int4 launch_kernel: kernels/int4_wmma.cu:148-158,
  * kernels/int4_ptx_mma_k64_x4_x2nontrans_ca.cu:168-178.
- * The operands are widened to int8 in `workspace` (tcg_gemm_s4_workspace_size
- * bytes, 256-byte aligned) and multiplied by the int8 tensor-core path.  With
- * workspace == NULL the library takes stream-ordered memory from the
- * device's default memory pool for the duration of the call. */
+ * One kernel: TMA brings the packed rows into shared memory, converter warps
+ * widen them to int8 there, and the int8 tensor-core path multiplies them --
+ * like the reference's launch_kernel it allocates nothing, and `workspace`
+ * may be NULL.  `workspace` (tcg_gemm_s4_workspace_size bytes, 256-byte
+ * aligned) is used only by the two-pass form (operands widened into it by a
+ * separate kernel, then the int8 GEMM), which the environment variable
+ * TCG_S4_PREPASS=1 selects; in that form a NULL workspace is taken from a
+ * stream-ordered private memory pool for the duration of the call. */
 size_t tcg_gemm_s4_workspace_size(int M, int N, int K, int batches);
 tcg_status tcg_gemm_s4(const int8_t* A_packed, const int8_t* BT_packed, int32_t* C,
                        int M, int N, int K, int batches,
@@ -125,7 +129,7 @@ tcg_status tcg_quantize_absmax_s4(const float* src, int8_t* dst_packed, int rows
                                   void* stream);
 
 /* Widen packed int4 to int8 (low nibble first), n_packed bytes -> 2*n_packed.
- * The first stage of tcg_gemm_s4, exposed for reuse. */
+ * The first pass of tcg_gemm_s4's two-pass form, exposed for reuse. */
 tcg_status tcg_unpack_s4(const int8_t* packed, int8_t* out, size_t n_packed, void* stream);
 
 /* No counterpart in the reference.  tcg_gemm_s4 without allocation.
@@ -135,10 +139,13 @@ tcg_status tcg_unpack_s4(const int8_t* packed, int8_t* out, size_t n_packed, voi
  * plugins to allocate, or a latency-critical path that cannot accept the
  * device-wide synchronisation cudaMalloc implies, or code written to the
  * reference's int4 `launch_kernel` contract, which takes no workspace and
- * allocates nothing.  tcg_gemm_s4 needs scratch for the widened operands, so
- * for those callers this variant keeps it in one fixed device array inside
- * libtcgemm.so, TCG_S4_STATIC_SCRATCH_BYTES large, that every GPU which loads
- * the library holds until the process exits.
+ * allocates nothing.  tcg_gemm_s4's two-pass form needs scratch for the
+ * widened operands, so for those callers this variant runs that form with
+ * its scratch in one fixed device array inside libtcgemm.so,
+ * TCG_S4_STATIC_SCRATCH_BYTES large, that every GPU which loads the library
+ * holds until the process exits.  (tcg_gemm_s4's default fused kernel
+ * allocates nothing either; this entry keeps the two-pass form available to
+ * such callers, e.g. as an independent cross-check.)
  *
  * Same operands, result and status codes as tcg_gemm_s4.  The limit is on
  * the scratch need, tcg_gemm_s4_workspace_size(M, N, K, batches) <=

@@ -89,8 +89,9 @@ float SolverInt8::run(const int8_t* d_A, const int8_t* d_BT, int32_t* d_C)
 
 #elif defined(TCG_COMPAT_S4)
 
-// The reference's int4 signature has no workspace; the widened operands are
-// taken from libtcgemm's stream-ordered private pool (workspace == NULL).
+// The reference's int4 signature has no workspace, and its launch_kernel
+// allocates nothing (kernels/int4_wmma.cu:148-158); neither does this one:
+// the int4 kernel widens the packed operands in shared memory.
 void launch_kernel(const int8_t* A, const int8_t* BT, int32_t* C, const GemmConfig& cfg, cudaStream_t stream)
 {
     die_on(tcg_gemm_s4(A, BT, C, cfg.M, cfg.N, cfg.K, cfg.num_batches, nullptr, 0, stream),

@@ -80,6 +80,9 @@ template <int kKind, bool kAccF16, bool kBMn, int kBN, int kStages, int kShape>
 struct GemmTraits {
     static constexpr bool kPair = kShape == kShapePair || kShape == kShapePairWide;  // cta_group::2
     static constexpr bool kWide = kShape == kShapeWide || kShape == kShapePairWide;  // two A blocks per CTA
+    // packed int4: TMA brings 64 bytes of packed K per row into a staging
+    // ring; converter warps widen them into the int8 ring the MMAs read
+    static constexpr bool kI4 = kKind == kKindI4;
     static constexpr int kElem = kKind == kKindF16 ? 2 : 1;
     static constexpr int kBK = kBKBytes / kElem;      // K elements per stage
     static constexpr int kUmmaK = 32 / kElem;         // K per instruction (32 bytes)
@@ -99,16 +102,31 @@ struct GemmTraits {
     static constexpr int kAtomN = kBKBytes / kElem;
     static constexpr int kBoxBytesMn = kBK * kBKBytes;
     static constexpr int kEpiArrivals = kPair ? 8 : 4;  // one per epilogue warp (of both CTAs)
+    static constexpr int kConvWarps = kI4 ? 8 : 0;       // int4 converter warps per CTA
+    static constexpr int kThreadCount = kThreads + 32 * kConvWarps;
     static constexpr int kRing = 4;                      // work-item ring entries
-    static constexpr int kRingConsumers = kPair ? 10 : 5;  // arrivals per ring entry (see the kernel)
+    // arrivals per ring entry: the MMA issuer, every epilogue (and converter)
+    // warp of both CTAs, and a pair's second producer (see the kernel)
+    static constexpr int kRingConsumers = (kPair ? 10 : 5) + (kPair ? 2 : 1) * kConvWarps;
+    // arrivals that fill an int8 ring stage: the TMA transaction (one arrive
+    // with expect_tx); int4: every converter warp of the CTA, and for a pair
+    // the leader's producer announcing the second CTA's 16-byte signal copy
+    static constexpr int kFullArrivals = kI4 ? kConvWarps + (kPair ? 1 : 0) : 1;
+    static constexpr int kSignalBytes = 16;  // int4 pair: second CTA's "stage converted" copy
     static constexpr int kBarrierBytes = 512;
     // two 32 x 32 word staging tiles (4 KB each) per epilogue warp
     static constexpr int kEpiStageBytes = 4 * 2 * 32 * 32 * 4;
+    // int4: the TMA lands a stage's packed rows (64 bytes each) in the upper
+    // half of the same ring stage; one barrier per stage counts those bytes
+    static constexpr int kPkOffset = kStageBytes / 2;
+    static constexpr int kPkStages = kI4 ? kStages : 0;
+    static constexpr int kConvRows = kASub * kBM + kBRows;  // rows of a stage (A blocks, then B)
     static constexpr int kSmemBytes = kStages * kStageBytes + kEpiStageBytes + 1024 + kBarrierBytes;
     static_assert(kBRows % kAtomN == 0 || !kBMn, "MN-major B needs whole 128-byte atoms");
     static_assert(kTmemCols >= 32 && kTmemCols <= 512, "TMEM allocation");
     static_assert(kSmemBytes <= 232448, "shared memory per CTA");
-    static_assert(8 * (2 * kStages + 6 + 2 * kRing) + 8 + 4 * kRing <= 384, "barrier area");
+    static_assert(!kI4 || (!kBMn && kConvRows % 32 == 0), "int4 staging");
+    static_assert(8 * (2 * kStages + 6 + 2 * kRing + kPkStages) + 8 + 4 * kRing <= 384, "barrier area");
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int& b, int& tm,
@@ -224,9 +242,15 @@ __device__ __forceinline__ uint32_t num_clusters_x()
 
 // Convert 32 accumulator words in place: fp16 accumulators (low halves) to
 // fp32, or int32 to fp32 scaled by the combined dequantisation factor.
-template <bool kAccF16>
+// kScaled16: int4 accumulators hold 256 x the product (both operands were
+// widened as 16 x value, see spread_word); the exact result is acc >> 8.
+template <bool kAccF16, bool kScaled16 = false>
 __device__ __forceinline__ void epi_convert(uint32_t (&v)[32], bool dequant, float combined)
 {
+    if constexpr (kScaled16) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = static_cast<uint32_t>(static_cast<int32_t>(v[j]) >> 8);
+    }
     if constexpr (kAccF16) {
 #pragma unroll
         for (int j = 0; j < 32; ++j)
@@ -283,6 +307,90 @@ __device__ __forceinline__ void epi_store_peers(const GemmParams& p, const uint3
     }
 }
 
+// Widen four packed int4 bytes (two values per byte, low nibble first) to
+// eight int8 values.  A nibble x (two's complement, 4 bits) has the value
+// (x ^ 8) - 8.  With x ^ 0x88 every byte lies in [0x80, 0x8f], so subtracting
+// 0x08 from all four bytes at once borrows across none of them and leaves
+// 0x80 + value; the final ^ 0x80 (after interleaving) removes the bias.  Nine
+// integer operations for eight values (no byte-SIMD emulation).
+__device__ __forceinline__ void widen_word(uint32_t w, uint32_t& o0, uint32_t& o1)
+{
+    const uint32_t lo = ((w & 0x0F0F0F0Fu) ^ 0x88888888u) - 0x08080808u;
+    const uint32_t hi = (((w >> 4) & 0x0F0F0F0Fu) ^ 0x88888888u) - 0x08080808u;
+    o0 = __byte_perm(lo, hi, 0x5140) ^ 0x80808080u;  // lo0 hi0 lo1 hi1
+    o1 = __byte_perm(lo, hi, 0x7362) ^ 0x80808080u;  // lo2 hi2 lo3 hi3
+}
+
+// The converter's widening: four packed bytes (eight int4 values, k = 0..7,
+// low nibble first) become two words of int8 holding 16 x value -- the even
+// k (low nibbles shifted into the high half of each byte) in `ev`, the odd k
+// (high nibbles, masked in place) in `od`.  Two's-complement nibbles need no
+// sign extension this way (the nibble's sign bit is the byte's), three
+// integer operations for eight values.  Both operands go through the same
+// function, so the K order inside each 32-value group is the same permutation
+// for A and B and the dot products are unchanged; every product is 256 x the
+// int4 product, which the epilogue divides out exactly (acc >> 8).  The
+// int32 accumulator holds K x 2^14 at most: K < 131072.
+__device__ __forceinline__ void spread_word(uint32_t w, uint32_t& ev, uint32_t& od)
+{
+    ev = (w << 4) & 0xF0F0F0F0u;
+    od = w & 0xF0F0F0F0u;
+}
+
+// int4 stage conversion, in place, by the kConv threads of the converter
+// warps (thread ct).  The TMA put the stage's `rows` packed rows (64 bytes =
+// 128 K values each, back to back) in the upper half of the ring stage; they
+// are spread (spread_word) into the whole stage in the layout a
+// 128-byte-swizzled TMA load
+// would have produced (row r at r * 128, 16-byte chunk c stored at chunk
+// c ^ (r & 7)), which the MMA descriptors read.  Phase 1 (conv_load) reads
+// each thread's packed chunks into registers; after a barrier of the
+// converter warps, phase 2 (conv_store) writes them, so no write reaches
+// packed bytes another thread has yet to read.  Every 8 consecutive threads
+// read two consecutive packed rows (128 contiguous bytes) and write chunks of
+// two rows whose swizzled positions are disjoint: no bank conflicts.
+template <int kConv, int kMaxRows>
+struct ConvPlan {
+    static constexpr int kStep = kConv >= 4 ? kConv / 4 : 1;  // rows per pass
+    static constexpr int kPasses = (kMaxRows + kStep - 1) / kStep;
+};
+
+template <int kConv, int kMaxRows>
+__device__ __forceinline__ void conv_load(const uint8_t* src, int rows, int ct,
+                                          uint4 (&v)[ConvPlan<kConv, kMaxRows>::kPasses])
+{
+    using P = ConvPlan<kConv, kMaxRows>;
+    const int j = ct & 3;
+#pragma unroll
+    for (int u = 0; u < P::kPasses; ++u) {
+        const int r = u * P::kStep + (ct >> 2);
+        if (r < rows) v[u] = *reinterpret_cast<const uint4*>(src + r * 64 + j * 16);
+    }
+}
+
+template <int kConv, int kMaxRows>
+__device__ __forceinline__ void conv_store(uint8_t* dst, int rows, int ct,
+                                           const uint4 (&v)[ConvPlan<kConv, kMaxRows>::kPasses])
+{
+    using P = ConvPlan<kConv, kMaxRows>;
+    const int j = ct & 3;  // 16-byte packed chunk = int8 chunks 2j, 2j+1
+#pragma unroll
+    for (int u = 0; u < P::kPasses; ++u) {
+        const int r = u * P::kStep + (ct >> 2);
+        if (r < rows) {
+            uint4 a, b;
+            spread_word(v[u].x, a.x, a.y);
+            spread_word(v[u].y, a.z, a.w);
+            spread_word(v[u].z, b.x, b.y);
+            spread_word(v[u].w, b.z, b.w);
+            uint8_t* row = dst + r * 128;
+            const int sw = r & 7;
+            *reinterpret_cast<uint4*>(row + (((2 * j) ^ sw) << 4)) = a;
+            *reinterpret_cast<uint4*>(row + (((2 * j + 1) ^ sw) << 4)) = b;
+        }
+    }
+}
+
 // kPair = false: one CTA per 128 x kBN tile, tcgen05 cta_group::1.
 // kPair = true : a cluster of two CTAs per 256 x kBN tile, tcgen05
 //   cta_group::2.  CTA r holds rows [128r, 128r+128) of A and columns
@@ -292,7 +400,7 @@ __device__ __forceinline__ void epi_store_peers(const GemmParams& p, const uint3
 //   barriers; the leader's commits arrive on both CTAs' empty / tmem-full
 //   barriers; both epilogues release the accumulator on the leader's barrier.
 template <int kKind, bool kAccF16, bool kBMn, int kBN, int kStages, int kShape>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages, kShape>::kThreadCount, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmC,
                 const GemmParams p)
@@ -304,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint32_t* epi_stage = reinterpret_cast<uint32_t*>(smem + kStages * T::kStageBytes);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * T::kStageBytes + T::kEpiStageBytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(epi_stage) + T::kEpiStageBytes);
     uint64_t* full = bars;
     uint64_t* empty = bars + kStages;
     uint64_t* tfull = bars + 2 * kStages;
@@ -313,10 +421,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* qfull = drain + 1;          // work-item ring: entry published
     uint64_t* qempty = qfull + T::kRing;  // work-item ring: entry read by every consumer (leader CTA's)
     uint64_t* clcbar = qempty + T::kRing; // cluster launch control response landed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(clcbar + 1);
+    uint64_t* full_pk = clcbar + 1;       // int4: a stage's packed rows landed (TMA, this CTA)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full_pk + T::kPkStages);
     volatile uint32_t* abort_flag = tmem_slot + 1;
     volatile int* ring = reinterpret_cast<volatile int*>(tmem_slot + 2);
     const uint32_t clc_resp = smem_u32(reinterpret_cast<uint8_t*>(bars) + 384);  // 16 bytes, 16-aligned
+    const uint32_t sig_buf = smem_u32(reinterpret_cast<uint8_t*>(bars) + 400);   // 16 bytes, 16-aligned
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -329,9 +439,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&full[s]), T::kFullArrivals);
             mbar_init(smem_u32(&empty[s]), 1);
         }
+        for (int s = 0; s < T::kPkStages; ++s) mbar_init(smem_u32(&full_pk[s]), 1);
         for (int a = 0; a < 2; ++a) {
             mbar_init(smem_u32(&tfull[a]), 1);
             mbar_init(smem_u32(&tempty[a]), T::kEpiArrivals);
@@ -372,6 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // producer bookkeeping for the abort drain: per stage, a load was issued /
     // the parity of its phase; a cluster-launch-control response in flight
     uint32_t issued = 0, issued_parity = 0;
+    bool signalled = false;  // int4 pair, second CTA: a signal copy into the leader was sent
     bool clc_pending = false;
     uint32_t clc_phase = 0;
 
@@ -463,6 +575,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool reverse = p.k_alternate && ((t / p.wave_units) & 1);
             for (int kb = 0; kb < p.num_kb; ++kb) {
                 const int kc = reverse ? p.num_kb - 1 - kb : kb;
+                if constexpr (T::kI4) {
+                    // packed rows (64 bytes of K each) into the upper half of
+                    // this CTA's ring stage once the MMAs have released it,
+                    // completing on this CTA's barrier: the converter warps of
+                    // the same CTA widen them in place
+                    if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.timeout_ns,
+                                      (blockIdx.x << 8) | 0x10u | stage)) {
+                        aborted = true;
+                        break;
+                    }
+                    if (kPair && leader)  // the second CTA's converters signal with a 16-byte copy
+                        mbar_arrive_expect_tx(smem_u32(&full[stage]), T::kSignalBytes);
+                    const uint32_t fb = smem_u32(&full_pk[stage]);
+                    const uint32_t dst = stage0 + stage * T::kStageBytes + T::kPkOffset;
+                    const int b_rows = half < 0 ? T::kBRows : T::kBRows / 2;
+                    mbar_arrive_expect_tx(fb, static_cast<uint32_t>((T::kASub * kBM + b_rows) * 64));
+#pragma unroll
+                    for (int h = 0; h < T::kASub; ++h)
+                        tma_load_3d(dst + h * kBM * 64, &tmA, fb, kc * 64, a_row + h * kBM, b);
+                    tma_load_3d(dst + T::kASub * kBM * 64, mapB, fb, kc * 64, b_row, b);
+                    issued |= 1u << stage;
+                    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                    continue;
+                }
                 const uint32_t fb_local = smem_u32(&full[stage]);
                 if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.timeout_ns,
                                   (blockIdx.x << 8) | 0x10u | stage)) {
@@ -569,6 +709,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (threadIdx.x == 32 && leader) {
         // -------------------------------------------------- MMA issuer ----
+        // int4 pairs: the second CTA's converter warps fill its half of each
+        // stage and arrive (release, cluster scope) on these barriers
+        constexpr bool kFullCluster = T::kI4 && kPair;
         int stage = 0;
         uint32_t phase = 0;
         bool aborted = false;
@@ -635,8 +778,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int st = stage;
                 uint32_t ph = phase;
                 for (int kb = 0; kb < pre; ++kb) {
-                    if (!wait_bounded(smem_u32(&full[st]), ph, abort_flag, p.timeout_ns,
-                                      (blockIdx.x << 8) | 0x30u | st)) {
+                    if (!wait_bounded<kFullCluster>(smem_u32(&full[st]), ph, abort_flag, p.timeout_ns,
+                                                    (blockIdx.x << 8) | 0x30u | st)) {
                         aborted = true;
                         break;
                     }
@@ -661,8 +804,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 kb0 = pre;
             }
             for (int kb = kb0; kb < p.num_kb; ++kb) {
-                if (!wait_bounded(smem_u32(&full[stage]), phase, abort_flag, p.timeout_ns,
-                                  (blockIdx.x << 8) | 0x30u | stage)) {
+                if (!wait_bounded<kFullCluster>(smem_u32(&full[stage]), phase, abort_flag, p.timeout_ns,
+                                                (blockIdx.x << 8) | 0x30u | stage)) {
                     aborted = true;
                     break;
                 }
@@ -689,7 +832,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
             }
         }
-    } else if (warp >= 2) {
+    } else if (warp >= 2 && warp < 6) {
         // ---------------------------------------------------- epilogue ----
         // Each warp owns 32 rows of the tile (its TMEM lane quarter) and
         // reads them 64 columns per tcgen05 wait (two 32x32b.x32 loads: lane
@@ -709,7 +852,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int csub = lane & 7;   // 16-byte chunk (4 columns) within the 32 columns
         // dequantising epilogue: the per-tensor scales were produced on the
         // device by an earlier launch on the same stream
-        const bool dequant = kKind == kKindI8 && p.scale_a != nullptr;
+        const bool dequant = (kKind == kKindI8 || kKind == kKindI4) && p.scale_a != nullptr;
         const float combined = dequant ? __fmul_rn(*p.scale_a, *p.scale_b) : 0.f;
         uint32_t nstore = 0;  // TMA stores issued by this warp (selects the staging tile)
         int local = 0;
@@ -748,8 +891,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld_32x32b_x32(t_addr + c, va);
                     tmem_ld_32x32b_x32(t_addr + c + 32, vb);
                     tmem_ld_wait();
-                    epi_convert<kAccF16>(va, dequant, combined);
-                    epi_convert<kAccF16>(vb, dequant, combined);
+                    epi_convert<kAccF16, T::kI4>(va, dequant, combined);
+                    epi_convert<kAccF16, T::kI4>(vb, dequant, combined);
                     epi_store_tma(&tmC, stile + (nstore & 1u) * 1024, stile_s + (nstore & 1u) * 4096, va, lane,
                                   col, row0, b);
                     if (p.n_extra > 0) epi_store_peers(p, stile + (nstore & 1u) * 1024, row0, col, cbase, lane);
@@ -770,7 +913,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(t_addr + c, v);
                 tmem_ld_wait();
-                epi_convert<kAccF16>(v, dequant, combined);
+                epi_convert<kAccF16, T::kI4>(v, dequant, combined);
 #pragma unroll
                 for (int q = 0; q < 8; ++q)
                     *reinterpret_cast<uint4*>(stile + lane * 32 + ((q ^ (lane & 7)) << 2)) =
@@ -831,6 +974,68 @@ __global__ void __launch_bounds__(kThreads, 1)
         // memory with them); the writes to C complete with the grid
         if (lane == 0 && nstore) bulk_wait_group_read<0>();
         __syncwarp();
+    } else if (T::kI4 && warp >= 6) {
+        // --------------------------------------------- int4 converters ----
+        // Per k-block: wait for the stage's packed rows (this CTA's TMA, issued
+        // once the MMAs had released the stage), widen them in place, make
+        // the writes visible to the tensor core (async proxy), then report the
+        // int8 stage filled on the leader's barrier, which the MMA issuer
+        // waits on: the leader's converter warps arrive on it; a pair's second
+        // CTA, once all its converter warps are done (named barrier 2), sends
+        // one 16-byte copy into the leader's shared memory that completes on
+        // it -- a remote arrive with cluster-scope release would stall each
+        // warp for about a microsecond.  Every wait outcome goes through a
+        // barrier-AND of the converter warps (named barrier 1), so they give
+        // up together and none is left waiting at a barrier.
+        constexpr int kConv = 32 * T::kConvWarps;
+        using Plan = ConvPlan<kConv, T::kConvRows>;
+        const int ct = (warp - 6) * 32 + lane;  // 0 .. kConv - 1
+        const uint32_t full_leader0 = kPair ? mapa_shared(smem_u32(&full[0]), 0) : smem_u32(&full[0]);
+        int ss = 0;
+        uint32_t sph = 0;
+        for (;;) {
+            const bool got = wait_bounded_warp<kPair>(smem_u32(&qfull[q]), qph, abort_flag, p.timeout_ns,
+                                                      (blockIdx.x << 8) | 0x7Bu);
+            if (!named_barrier_and(1, kConv, got)) break;
+            const int t = ring[q];
+            __syncwarp();
+            if (lane == 0) ring_release();
+            ring_next();
+            if (t < 0) break;
+            int b, tm, tn, half;
+            work_coords(t, p.split_from, p.tiles_m, p.tiles_n, p.group_m, b, tm, tn, half);
+            const int rows = T::kASub * kBM + (half < 0 ? T::kBRows : T::kBRows / 2);
+            bool ok = true;
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                uint8_t* stage_ptr = smem + ss * T::kStageBytes;
+                const bool landed = wait_bounded_warp(smem_u32(&full_pk[ss]), sph, abort_flag, p.timeout_ns,
+                                                      (blockIdx.x << 8) | 0xA0u | ss);
+                uint4 v[Plan::kPasses];
+                if (landed) conv_load<kConv, T::kConvRows>(stage_ptr + T::kPkOffset, rows, ct, v);
+                if (!named_barrier_and(1, kConv, landed)) {  // every packed byte read (or all give up)
+                    ok = false;
+                    break;
+                }
+                conv_store<kConv, T::kConvRows>(stage_ptr, rows, ct, v);
+                fence_proxy_async_smem();
+                const uint32_t fb = full_leader0 + static_cast<uint32_t>(ss * sizeof(uint64_t));
+                if (kPair && !leader) {
+                    named_barrier_and(2, kConv, true);  // every converter warp's stores fenced
+                    if (ct == 0) {
+                        bulk_copy_to_cluster(mapa_shared(sig_buf, 0), sig_buf, T::kSignalBytes, fb);
+                        signalled = true;
+                    }
+                } else {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(fb);
+                }
+                if (++ss == kStages) {
+                    ss = 0;
+                    sph ^= 1u;
+                }
+            }
+            if (!ok) break;
+        }
     }
 
     if (p.n_extra > 0) __threadfence_system();  // peer stores performed before the kernel ends
@@ -841,7 +1046,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Some role gave up.  Before shared and tensor memory are released,
         // let this CTA's own TMA copies land and its MMAs retire.
         if (threadIdx.x == 0 && issued) {
-            if (!kPair || leader) {
+            if constexpr (T::kI4) {  // packed loads complete on this CTA's own barriers
+                for (int s = 0; s < T::kPkStages; ++s)
+                    if (issued & (1u << s)) drain_wait(smem_u32(&full_pk[s]), (issued_parity >> s) & 1u);
+            } else if (!kPair || leader) {
                 for (int s = 0; s < kStages; ++s)
                     if (issued & (1u << s)) drain_wait(smem_u32(&full[s]), (issued_parity >> s) & 1u);
             } else {
@@ -853,6 +1061,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         if (threadIdx.x == 0 && clc_pending) drain_wait(smem_u32(clcbar), clc_phase);  // response in flight
+        if (signalled) {
+            // a signal copy may still be reading this CTA's shared memory: give
+            // it a fixed 2 ms, far above a copy's latency
+            const uint64_t t0 = global_timer_ns();
+            while (global_timer_ns() - t0 < 2000000ull) {
+            }
+        }
         if (threadIdx.x == 32 && leader) {
             if constexpr (kPair)
                 umma_commit_pair_local(smem_u32(drain));
@@ -895,18 +1110,6 @@ __global__ void wait_selftest_kernel(unsigned long long timeout_ns)
         wait_bounded_warp(smem_u32(&bar), 0, abort_flag, timeout_ns, 0xFEu);
     }
     __syncthreads();
-}
-
-// Widen packed int4 (two per byte, low nibble first) to int8, 16 packed bytes
-// per thread per step.
-__device__ __forceinline__ void widen_word(uint32_t w, uint32_t& o0, uint32_t& o1)
-{
-    uint32_t lo = w & 0x0F0F0F0Fu;
-    uint32_t hi = (w >> 4) & 0x0F0F0F0Fu;
-    lo = __vsub4(lo ^ 0x08080808u, 0x08080808u);  // sign-extend each nibble
-    hi = __vsub4(hi ^ 0x08080808u, 0x08080808u);
-    o0 = __byte_perm(lo, hi, 0x5140);  // lo0 hi0 lo1 hi1
-    o1 = __byte_perm(lo, hi, 0x7362);  // lo2 hi2 lo3 hi3
 }
 
 // Two tensors (A and B of an int4 GEMM) in one launch: 16-byte chunks

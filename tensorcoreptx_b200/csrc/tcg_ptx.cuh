@@ -13,6 +13,7 @@ namespace tcg {
 constexpr int kKindF16 = 0;  // fp16 x fp16 (kind::f16)
 constexpr int kKindI8 = 1;   // s8 x s8 -> s32 (kind::i8)
 constexpr int kKindF8 = 2;   // e4m3 / e5m2 -> f32 (kind::f8f6f4)
+constexpr int kKindI4 = 3;   // packed s4 operands, widened to s8 in shared memory (kind::i8)
 
 // ---------------------------------------------------------------- helpers --
 
@@ -77,6 +78,37 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
         : "r"(bar), "r"(parity)
         : "memory");
     return ok != 0;
+}
+
+// Copy `bytes` (a multiple of 16) from this CTA's shared memory to another
+// CTA's of the cluster, completing the bytes on an mbarrier there.  Used as a
+// non-blocking cross-CTA signal whose completion the hardware counts, like a
+// TMA load's.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, uint32_t src, uint32_t bytes,
+                                                     uint32_t bar_cluster)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            dst_cluster),
+        "r"(src), "r"(bytes), "r"(bar_cluster)
+        : "memory");
+}
+
+// Named barrier `id` over `nthreads` threads (whole warps) that also returns
+// the AND of every participant's `v`: the warps of one role agree on whether
+// all of them may go on, so none waits at a barrier that another has left.
+__device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t nthreads, bool v)
+{
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "barrier.cta.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
 }
 
 // ------------------------------------------- programmatic dependent launch --
@@ -197,7 +229,7 @@ template <int kKind>
 __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                  uint32_t accumulate)
 {
-    if constexpr (kKind == kKindI8) {
+    if constexpr (kKind == kKindI8 || kKind == kKindI4) {
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
             "setp.ne.b32 p, %4, 0;\n\t"
@@ -368,7 +400,7 @@ template <int kKind>
 __device__ __forceinline__ void umma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                       uint32_t accumulate)
 {
-    if constexpr (kKind == kKindI8) {
+    if constexpr (kKind == kKindI8 || kKind == kKindI4) {
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
             "setp.ne.b32 p, %4, 0;\n\t"

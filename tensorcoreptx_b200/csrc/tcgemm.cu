@@ -93,10 +93,11 @@ struct MapKey {
     uint64_t d0, d1, d2, s1, s2;
     uint32_t box0, box1;
     int dt;
+    int swz;
     bool operator==(const MapKey& o) const
     {
         return base == o.base && d0 == o.d0 && d1 == o.d1 && d2 == o.d2 && s1 == o.s1 && s2 == o.s2 &&
-               box0 == o.box0 && box1 == o.box1 && dt == o.dt;
+               box0 == o.box0 && box1 == o.box1 && dt == o.dt && swz == o.swz;
     }
 };
 struct MapCache {
@@ -109,13 +110,16 @@ struct MapCache {
 thread_local MapCache t_map_cache;
 
 tcg_status encode_3d_uncached(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
-                              uint64_t d2, uint64_t s1, uint64_t s2, uint32_t box0, uint32_t box1);
+                              uint64_t d2, uint64_t s1, uint64_t s2, uint32_t box0, uint32_t box1,
+                              CUtensorMapSwizzle swz);
 
-// 3-D tiled map: dims {d0 (contiguous), d1, d2}, byte strides of d1 and d2.
+// 3-D tiled map: dims {d0 (contiguous), d1, d2}, byte strides of d1 and d2;
+// 128-byte swizzle unless asked otherwise.
 tcg_status encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
-                     uint64_t d2, uint64_t s1, uint64_t s2, uint32_t box0, uint32_t box1)
+                     uint64_t d2, uint64_t s1, uint64_t s2, uint32_t box0, uint32_t box1,
+                     CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B)
 {
-    const MapKey k{base, d0, d1, d2, s1, s2, box0, box1, static_cast<int>(dt)};
+    const MapKey k{base, d0, d1, d2, s1, s2, box0, box1, static_cast<int>(dt), static_cast<int>(swz)};
     MapCache& c = t_map_cache;
     for (int i = 0; i < MapCache::kEntries; ++i) {
         if (c.used[i] && c.key[i] == k) {
@@ -123,7 +127,7 @@ tcg_status encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
             return TCG_SUCCESS;
         }
     }
-    const tcg_status s = encode_3d_uncached(map, dt, base, d0, d1, d2, s1, s2, box0, box1);
+    const tcg_status s = encode_3d_uncached(map, dt, base, d0, d1, d2, s1, s2, box0, box1, swz);
     if (s == TCG_SUCCESS) {
         const int i = c.next;
         c.next = (c.next + 1) % MapCache::kEntries;
@@ -135,14 +139,15 @@ tcg_status encode_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
 }
 
 tcg_status encode_3d_uncached(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
-                              uint64_t d2, uint64_t s1, uint64_t s2, uint32_t box0, uint32_t box1)
+                              uint64_t d2, uint64_t s1, uint64_t s2, uint32_t box0, uint32_t box1,
+                              CUtensorMapSwizzle swz)
 {
     cuuint64_t dims[3] = {d0, d1, d2};
     cuuint64_t strides[2] = {s1, s2};
     cuuint32_t box[3] = {box0, box1, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = g_encode(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         t_last_cuda_error = static_cast<int>(r);
@@ -265,6 +270,7 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     void* const* extra = epi.extra;
     const int n_extra = epi.n_extra;
     constexpr bool kPair = kShape == kShapePair || kShape == kShapePairWide;
+    // ring stages (int4 widens each stage in place: same depths as int8)
     constexpr int kStages = kShape == kShapeWide ? 3 : kShape == kShapePairWide ? 4
                             : kPair ? (kBN == 256 ? 6 : 8) : (kBN == 256 ? 4 : (kBN == 128 ? 6 : 8));
     constexpr bool kByte = kKind != kKindF16;
@@ -286,7 +292,22 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     const CUtensorMapDataType dt = kByte ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const uint64_t es = T::kElem;
     CUtensorMap mA, mB, mBh;  // mBh: B boxes of half the rows, for half tiles (K-major B)
-    tcg_status s = encode_3d(&mA, dt, A, K, M, batches, K * es, static_cast<uint64_t>(M) * K * es, T::kBK, kBM);
+    tcg_status s;
+    if constexpr (kKind == kKindI4) {
+        // packed operands (K / 2 bytes per row), 64-byte boxes (128 values of
+        // K), unswizzled: the converter warps lay out the int8 stage
+        const uint64_t kp = static_cast<uint64_t>(K) / 2;
+        s = encode_3d(&mA, dt, A, kp, M, batches, kp, static_cast<uint64_t>(M) * kp, 64, kBM,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (s == TCG_SUCCESS)
+            s = encode_3d(&mB, dt, B, kp, N, batches, kp, static_cast<uint64_t>(N) * kp, 64, T::kBRows,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (s == TCG_SUCCESS)
+            s = encode_3d(&mBh, dt, B, kp, N, batches, kp, static_cast<uint64_t>(N) * kp, 64, T::kBRows / 2,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (s != TCG_SUCCESS) return s;
+    } else {
+    s = encode_3d(&mA, dt, A, K, M, batches, K * es, static_cast<uint64_t>(M) * K * es, T::kBK, kBM);
     if (s != TCG_SUCCESS) return s;
     if (kBMn) {  // B is K x N, N contiguous; half tiles load fewer 128-byte atoms
         s = encode_3d(&mB, dt, B, N, K, batches, N * es, static_cast<uint64_t>(K) * N * es, T::kAtomN, T::kBK);
@@ -298,6 +319,7 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
                           T::kBRows / 2);
     }
     if (s != TCG_SUCCESS) return s;
+    }
 
     GemmParams p;
     p.C = C;
@@ -311,7 +333,7 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     p.num_kb = (K + T::kBK - 1) / T::kBK;
     p.group_m = choose_group_m(T::kTileM, kBN, kPair ? dev.sms / 2 : dev.sms, p.tiles_m);
     static const int env_kalt = env_int("TCG_K_ALT", 1);
-    p.k_alternate = (kKind == kKindI8 && env_kalt) ? 1 : 0;  // integer sums are order-free
+    p.k_alternate = ((kKind == kKindI8 || kKind == kKindI4) && env_kalt) ? 1 : 0;  // integer sums are order-free
     // Optional L2 eviction priorities for the A / B loads (-1 = no hint, the
     // default: on B200 the hinted loads doubled DRAM traffic at 32768^3).
     static const int env_l2a = env_int("TCG_L2_A", -1);
@@ -321,7 +343,7 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     p.n_extra = n_extra;
     // instruction descriptors of a whole tile (N = kBN) and of a half tile
     const auto idesc_for = [&](int n) {
-        if constexpr (kKind == kKindI8)
+        if constexpr (kKind == kKindI8 || kKind == kKindI4)
             return make_idesc(2u, 1u, 1u, kBMn, T::kUmmaM, n);  // S32 <- s8 x s8
         else if constexpr (kKind == kKindF8)
             return make_idesc(1u, epi.a_fmt, epi.b_fmt, kBMn, T::kUmmaM, n);  // F32 <- e4m3/e5m2
@@ -358,7 +380,7 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     std::memset(&cfg, 0, sizeof cfg);
     cudaLaunchAttribute attr[2];
     std::memset(attr, 0, sizeof attr);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(T::kThreadCount, 1, 1);
     cfg.dynamicSmemBytes = T::kSmemBytes;
     cfg.stream = st;
     cfg.attrs = attr;
@@ -629,18 +651,16 @@ size_t tcg_gemm_s4_workspace_size(int M, int N, int K, int batches)
 
 namespace {
 
-tcg_status gemm_s4_impl(const int8_t* A_packed, const int8_t* BT_packed, void* C, int M, int N, int K, int batches,
-                        void* workspace, size_t workspace_bytes, void* stream, const EpiArgs& epi)
+// int4 in two passes: both operands widened into scratch (A then B, 256-byte
+// aligned) by unpack_s4_kernel, then the int8 GEMM.  The scratch is the
+// caller's `workspace`, or, when that is NULL, a stream-ordered allocation
+// from the device's private pool.  tcg_gemm_s4_static runs this form with its
+// fixed device array; TCG_S4_PREPASS=1 selects it for tcg_gemm_s4 too.
+tcg_status gemm_s4_prepass(const int8_t* A_packed, const int8_t* BT_packed, void* C, int M, int N, int K,
+                           int batches, void* workspace, size_t workspace_bytes, cudaStream_t st,
+                           const EpiArgs& epi, DeviceState* dev)
 {
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    bool done;
-    tcg_status s = prologue(A_packed, BT_packed, C, M, N, K, batches, st, &done);
-    if (s != TCG_SUCCESS || done) return s;
-    if (K % 32 != 0) return TCG_ERR_SHAPE;
-    DeviceState* dev;
-    if ((s = device_state(&dev)) != TCG_SUCCESS) return s;
-    if ((s = resolve_encode()) != TCG_SUCCESS) return s;
-
+    tcg_status s;
     const size_t need = tcg_gemm_s4_workspace_size(M, N, K, batches);
     void* ws = workspace;
     bool owned = false;
@@ -676,6 +696,37 @@ tcg_status gemm_s4_impl(const int8_t* A_packed, const int8_t* BT_packed, void* C
         if (e != cudaSuccess && s == TCG_SUCCESS) s = cuda_fail(e);
     }
     return s;
+}
+
+// Validation shared by the int4 entries; *dev set when there is work.
+tcg_status s4_prologue(const int8_t* A_packed, const int8_t* BT_packed, void* C, int M, int N, int K, int batches,
+                       cudaStream_t st, bool* done, DeviceState** dev)
+{
+    tcg_status s = prologue(A_packed, BT_packed, C, M, N, K, batches, st, done);
+    if (s != TCG_SUCCESS || *done) return s;
+    if (K % 32 != 0) return TCG_ERR_SHAPE;
+    if ((s = device_state(dev)) != TCG_SUCCESS) return s;
+    return resolve_encode();
+}
+
+// int4 GEMM.  By default one fused kernel: TMA brings the packed operands
+// into a staging ring and converter warps widen them to int8 in shared
+// memory, next to the MMAs -- no scratch, no allocation, no second pass over
+// HBM.  The workspace arguments only matter for the two-pass form.
+tcg_status gemm_s4_impl(const int8_t* A_packed, const int8_t* BT_packed, void* C, int M, int N, int K, int batches,
+                        void* workspace, size_t workspace_bytes, void* stream, const EpiArgs& epi)
+{
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    bool done;
+    DeviceState* dev = nullptr;
+    tcg_status s = s4_prologue(A_packed, BT_packed, C, M, N, K, batches, st, &done, &dev);
+    if (s != TCG_SUCCESS || done) return s;
+    // the fused kernel's accumulators hold 256 x the result: K < 2^17 keeps
+    // them in int32; longer K takes the two-pass form
+    static const int env_prepass = env_int("TCG_S4_PREPASS");
+    if (env_prepass || K >= (1 << 17))
+        return gemm_s4_prepass(A_packed, BT_packed, C, M, N, K, batches, workspace, workspace_bytes, st, epi, dev);
+    return dispatch_bn<kKindI4, false, false>(*dev, A_packed, BT_packed, C, M, N, K, batches, st, epi);
 }
 
 }  // namespace
@@ -815,13 +866,16 @@ tcg_status tcg_gemm_s4_static(const int8_t* A_packed, const int8_t* BT_packed, i
 {
     if (M < 0 || N < 0 || K < 0 || batches < 0) return TCG_ERR_SHAPE;
     if (tcg_gemm_s4_workspace_size(M, N, K, batches) > TCG_S4_STATIC_SCRATCH_BYTES) return TCG_ERR_WORKSPACE;
-    DeviceState* dev;
-    tcg_status s = device_state(&dev);
-    if (s != TCG_SUCCESS) return s;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    bool done;
+    DeviceState* dev = nullptr;
+    tcg_status s = s4_prologue(A_packed, BT_packed, C, M, N, K, batches, st, &done, &dev);
+    if (s != TCG_SUCCESS || done) return s;
     void* ws = nullptr;
     if ((s = static_scratch(&ws)) != TCG_SUCCESS) return s;
-    // the caller-workspace path of tcg_gemm_s4: it allocates nothing
-    return tcg_gemm_s4(A_packed, BT_packed, C, M, N, K, batches, ws, TCG_S4_STATIC_SCRATCH_BYTES, stream);
+    // the two-pass form with the fixed array as its scratch: nothing is allocated
+    return gemm_s4_prepass(A_packed, BT_packed, C, M, N, K, batches, ws, TCG_S4_STATIC_SCRATCH_BYTES, st,
+                           EpiArgs(), dev);
 }
 
 tcg_status tcg_unpack_s4(const int8_t* packed, int8_t* out, size_t n_packed, void* stream)

@@ -120,8 +120,9 @@ def gemm_int4(A_packed: torch.Tensor, BT_packed: torch.Tensor,
               workspace: torch.Tensor | None = None) -> torch.Tensor:
     """C[M,N] int32 = A[M,K] int4 x BT[N,K]^T int4, both packed two per byte
     along K (low nibble = even k), i.e. int8 tensors of shape [M, K/2] and
-    [N, K/2].  `workspace` (uint8/int8, >= int4_workspace_size bytes) is
-    optional; without it a temporary is taken from torch's allocator."""
+    [N, K/2].  The kernel widens the packed operands in shared memory and
+    needs no scratch; `workspace` (>= int4_workspace_size bytes) is only used
+    by the two-pass form (TCG_S4_PREPASS=1)."""
     _check(A_packed.is_cuda and BT_packed.is_cuda, "A and BT must be CUDA tensors")
     _check(A_packed.dtype == torch.int8, "A must be int8 (packed int4)")
     _check(BT_packed.dtype == torch.int8, "BT must be int8 (packed int4)")
@@ -129,15 +130,12 @@ def gemm_int4(A_packed: torch.Tensor, BT_packed: torch.Tensor,
     _check(Kh == BT_packed.size(-1), "A cols must equal BT cols (both = K/2)")
     _check(A_packed.is_contiguous() and BT_packed.is_contiguous(), "A and BT must be contiguous")
     K = 2 * Kh
-    need = nat.lib().tcg_gemm_s4_workspace_size(M, N, K, batches)
-    if workspace is None:
-        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=A_packed.device)
-    _check(workspace.numel() * workspace.element_size() >= need, "workspace too small")
+    ws_ptr, ws_bytes = None, 0
+    if workspace is not None:
+        ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     C = _out(A_packed, M, N, batches, torch.int32)
     st = nat.lib().tcg_gemm_s4(A_packed.data_ptr(), BT_packed.data_ptr(), C.data_ptr(), M, N, K,
-                               batches, workspace.data_ptr(),
-                               workspace.numel() * workspace.element_size(),
-                               _stream_ptr(A_packed))
+                               batches, ws_ptr, ws_bytes, _stream_ptr(A_packed))
     nat.check("gemm_int4", st)
     return C
 
@@ -253,12 +251,10 @@ def gemm_int4_dequant(A_packed: torch.Tensor, BT_packed: torch.Tensor, scale_a: 
     _check(Kh == BT_packed.size(-1), "A cols must equal BT cols (both = K/2)")
     _check(A_packed.is_contiguous() and BT_packed.is_contiguous(), "A and BT must be contiguous")
     K = 2 * Kh
-    need = nat.lib().tcg_gemm_s4_workspace_size(M, N, K, batches)
-    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=A_packed.device)
     C = _out(A_packed, M, N, batches, torch.float32)
     st = nat.lib().tcg_gemm_s4_dequant(A_packed.data_ptr(), BT_packed.data_ptr(), C.data_ptr(), M, N, K,
-                                       batches, scale_a.data_ptr(), scale_b.data_ptr(), ws.data_ptr(),
-                                       ws.numel(), _stream_ptr(A_packed))
+                                       batches, scale_a.data_ptr(), scale_b.data_ptr(), None, 0,
+                                       _stream_ptr(A_packed))
     nat.check("gemm_int4_dequant", st)
     return C
 

@@ -71,3 +71,36 @@ def test_gemm_wait_expiry_aborts_cleanly(n, cta_mode):
         T.set_cta_pair(0)
     assert T.check_device_error() == 0
     assert freivalds_int8(A, BT, Cm)
+
+
+@pytest.mark.parametrize("cta_mode", [0, 1])
+def test_int4_gemm_wait_expiry_aborts_cleanly(cta_mode):
+    """The same for the fused int4 kernel, whose converter warps wait on the
+    packed staging ring and on the int8 ring's release: with a 2 us limit the
+    kernel reports TCG_ERR_TIMEOUT (or finishes), returns, and the next call
+    with the default limit is exact."""
+    from tensorcoreptx_b200 import _native as nat
+    import tensorcoreptx_b200 as T
+    L = nat.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    n = 4096
+    g = torch.Generator(device="cuda").manual_seed(41 + cta_mode)
+    Ap = torch.randint(-128, 128, (n, n // 2), generator=g, device="cuda", dtype=torch.int8)
+    Bp = torch.randint(-128, 128, (n, n // 2), generator=g, device="cuda", dtype=torch.int8)
+    torch.cuda.synchronize()
+    assert L.tcg_check_device_error(stream, None) == 0
+    T.set_cta_pair(cta_mode)
+    try:
+        L.tcg_set_wait_timeout_ns(2000)
+        T.gemm_int4(Ap, Bp)
+        st = L.tcg_check_device_error(stream, None)
+    finally:
+        L.tcg_set_wait_timeout_ns(0)
+        T.set_cta_pair(0)
+    assert st in (0, nat.TCG_ERR_TIMEOUT), st
+    torch.cuda.synchronize()
+    assert L.tcg_check_device_error(stream, None) == 0
+    C4 = T.gemm_int4(Ap, Bp)
+    C8 = T.gemm_int8(T.unpack_int4(Ap), T.unpack_int4(Bp))
+    assert T.check_device_error() == 0
+    assert torch.equal(C4, C8)
