@@ -61,7 +61,70 @@ struct GemmParams {
     int dynamic;               // 1: one cluster per work item, taken over by cluster launch control
     int wave_units;            // units (CTAs or pairs) resident at once
     unsigned long long timeout_ns;
+    // stream-K split (two-CTA 512 x 256 tiles): unit u of sk_units takes
+    // k-blocks [u*W/U, (u+1)*W/U) of the W = tiles * num_kb laid end to end
+    int sk;
+    int sk_units;
+    long long sk_work;
+    unsigned int sk_epoch;     // this launch's tag on the hand-off flags
+    int sk_slot;               // this launch's row of flags
 };
+
+// Stream-K hand-off flags: a unit that computed the first k-blocks of a tile
+// ("head") stores its raw accumulators into the tile's place in C, then sets
+// its flag (one per CTA rank and epilogue warp) to the launch's tag; the
+// unit that finishes the tile ("tail") waits for that flag, loads the
+// partial back into tensor memory, resets the flag and continues.  Slots
+// separate launches that may run at the same time.
+constexpr int kSkSlots = 64;
+constexpr int kSkMaxUnits = 256;
+__device__ unsigned int g_sk_flag[kSkSlots * kSkMaxUnits * 8];
+
+// A work item: tile t (or -1: no more work), k-blocks [kb0, kb1) of it, and
+// what the unit does with its accumulators.
+constexpr int kItemFull = 0;  // a whole tile: zero-initialised accumulate, store C
+constexpr int kItemHead = 1;  // first k-blocks: store raw accumulators, signal
+constexpr int kItemTail = 2;  // last k-blocks: load the head's partial first, store C
+struct WorkItem {
+    int t, kb0, kb1, kind, unit;
+};
+
+// Item i of stream-K unit u (false past its last).  A unit's range starts
+// inside tile t0 at k-block x0 and ends inside tile t1 at x1; it runs the
+// head of t1 first, then its whole tiles, then the tail of t0 last, so a
+// tail's partial was produced at the very start of the previous unit.
+__device__ __forceinline__ bool sk_item(const GemmParams& p, int u, int i, WorkItem& w)
+{
+    const long long kb = p.num_kb;
+    const long long s = static_cast<long long>(u) * p.sk_work / p.sk_units;
+    const long long e = static_cast<long long>(u + 1) * p.sk_work / p.sk_units;
+    const int t0 = static_cast<int>(s / kb), x0 = static_cast<int>(s % kb);
+    const int t1 = static_cast<int>(e / kb), x1 = static_cast<int>(e % kb);
+    const int first_full = x0 ? t0 + 1 : t0;
+    const int n_full = t1 > first_full ? t1 - first_full : 0;
+    w.unit = u;
+    if (x1) {
+        if (i == 0) {
+            w.t = t1, w.kb0 = 0, w.kb1 = x1, w.kind = kItemHead;
+            return true;
+        }
+        --i;
+    }
+    if (i < n_full) {
+        w.t = first_full + i, w.kb0 = 0, w.kb1 = p.num_kb, w.kind = kItemFull;
+        return true;
+    }
+    if (x0 && i == n_full) {
+        w.t = t0, w.kb0 = x0, w.kb1 = p.num_kb, w.kind = kItemTail;
+        return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ unsigned int* sk_flag(const GemmParams& p, int unit, int slot_in_unit)
+{
+    return &g_sk_flag[(p.sk_slot * kSkMaxUnits + unit) * 8 + slot_in_unit];
+}
 
 // Tile shapes: one CTA per 128 x BN tile (single), a 2-CTA cluster per
 // 256 x BN tile (pair, cta_group::2), one CTA per 256 x BN tile with two
@@ -126,7 +189,8 @@ struct GemmTraits {
     static_assert(kTmemCols >= 32 && kTmemCols <= 512, "TMEM allocation");
     static_assert(kSmemBytes <= 232448, "shared memory per CTA");
     static_assert(!kI4 || (!kBMn && kConvRows % 32 == 0), "int4 staging");
-    static_assert(8 * (2 * kStages + 6 + 2 * kRing + kPkStages) + 8 + 4 * kRing <= 384, "barrier area");
+    static constexpr int kRingInts = 4;  // t, kb0, kb1, kind | unit << 8
+    static_assert(8 * (2 * kStages + 6 + 2 * kRing + kPkStages) + 8 + 4 * kRingInts * kRing <= 384, "barrier area");
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int& b, int& tm,
@@ -269,7 +333,8 @@ __device__ __forceinline__ void epi_convert(uint32_t (&v)[32], bool dequant, flo
 // Two staging tiles per warp alternate; before one is rewritten, the store
 // that last read it (two stores ago) must have finished reading.
 __device__ __forceinline__ void epi_store_tma(const CUtensorMap* tmC, uint32_t* buf, uint32_t buf_s,
-                                              const uint32_t (&v)[32], int lane, int col, int row, int b)
+                                              const uint32_t (&v)[32], int lane, int col, int row, int b,
+                                              bool reduce = false)
 {
     if (lane == 0) bulk_wait_group_read<1>();
     __syncwarp();
@@ -280,7 +345,10 @@ __device__ __forceinline__ void epi_store_tma(const CUtensorMap* tmC, uint32_t* 
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-        tma_store_3d(tmC, buf_s, col, row, b);
+        if (reduce)
+            tma_reduce_add_3d(tmC, buf_s, col, row, b);
+        else
+            tma_store_3d(tmC, buf_s, col, row, b);
         bulk_commit_group();
     }
 }
@@ -501,13 +569,42 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
             qph ^= 1u;
         }
     };
-    // a consumer has read entry q: release it on the leader's barrier
+    // Entry q holds a WorkItem as four ints.  The scheduler writes it into
+    // this CTA's ring and, for a pair, the peer's (then arrives on both
+    // entry-full barriers; cluster-scope release for the peer's copy).
+    const auto ring_put = [&](const WorkItem& w) {
+        const int e[4] = {w.t, w.kb0, w.kb1, w.kind | (w.unit << 8)};
+#pragma unroll
+        for (int i = 0; i < T::kRingInts; ++i) ring[q * T::kRingInts + i] = e[i];
+        if constexpr (kPair) {
+#pragma unroll
+            for (int i = 0; i < T::kRingInts; ++i)
+                st_cluster_u32(mapa_shared(smem_u32((const void*)&ring[q * T::kRingInts + i]), 1),
+                               static_cast<uint32_t>(e[i]));
+            mbar_arrive_cluster_release(mapa_shared(smem_u32(&qfull[q]), 1));
+        }
+        mbar_arrive(smem_u32(&qfull[q]));
+    };
+    const auto ring_get = [&]() {
+        WorkItem w;
+        w.t = ring[q * T::kRingInts + 0];
+        w.kb0 = ring[q * T::kRingInts + 1];
+        w.kb1 = ring[q * T::kRingInts + 2];
+        const int ku = ring[q * T::kRingInts + 3];
+        w.kind = ku & 0xFF;
+        w.unit = ku >> 8;
+        return w;
+    };
+    // a consumer has read entry q: release it on the leader's barrier.  The
+    // read it releases is of this CTA's own shared memory and its value is
+    // already in a register, so a CTA-scope release suffices; a
+    // cluster-scope one would stall the thread about a microsecond per item.
     const auto ring_release = [&]() {
         if constexpr (kPair) {
             if (leader)
                 mbar_arrive(smem_u32(&qempty[q]));
             else
-                mbar_arrive_cluster_release(mapa_shared(smem_u32(&qempty[q]), 0));
+                mbar_arrive_cluster(mapa_shared(smem_u32(&qempty[q]), 0));
         } else {
             mbar_arrive(smem_u32(&qempty[q]));
         }
@@ -524,22 +621,20 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
         const uint64_t pol_b = l2_policy(p.l2_b);
         bool clc_live = p.dynamic != 0;  // the grid may still hold clusters to take over
         int t = unit;
+        int sk_i = 0;  // stream-K: this unit's next item
+        WorkItem cur{t, 0, p.num_kb, kItemFull, unit};
+        if (p.sk && !sk_item(p, unit, 0, cur)) cur.t = -1;
         for (;; ++local) {
             if (leader) {
-                // publish t (scheduler)
+                // publish the item (scheduler)
                 if (!wait_bounded(smem_u32(&qempty[q]), qph ^ 1u, abort_flag, p.timeout_ns,
                                   (blockIdx.x << 8) | 0x70u | q)) {
                     aborted = true;
                     break;
                 }
-                ring[q] = t;
-                if constexpr (kPair) {
-                    st_cluster_u32(mapa_shared(smem_u32((const void*)&ring[q]), 1), static_cast<uint32_t>(t));
-                    mbar_arrive_cluster_release(mapa_shared(smem_u32(&qfull[q]), 1));
-                }
-                mbar_arrive(smem_u32(&qfull[q]));
+                ring_put(cur);
                 ring_next();
-                if (t < 0) break;
+                if (cur.t < 0) break;
                 if (clc_live) {  // ask for the next work item now; the answer is read after this tile's loads
                     mbar_arrive_expect_tx(smem_u32(clcbar), 16);
                     clc_try_cancel(clc_resp, smem_u32(clcbar));
@@ -552,11 +647,12 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
                     aborted = true;
                     break;
                 }
-                t = ring[q];
+                cur = ring_get();
                 ring_release();
                 ring_next();
-                if (t < 0) break;
+                if (cur.t < 0) break;
             }
+            t = cur.t;
             int b, tm, tn, half;
             work_coords(t, p.split_from, p.tiles_m, p.tiles_n, p.group_m, b, tm, tn, half);
             const int a_row = tm * T::kTileM + static_cast<int>(rank) * (T::kASub * kBM);
@@ -573,8 +669,8 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
             // brought into L2.  Integer accumulation is exact in any order;
             // floating-point kinds keep one order.
             const bool reverse = p.k_alternate && ((t / p.wave_units) & 1);
-            for (int kb = 0; kb < p.num_kb; ++kb) {
-                const int kc = reverse ? p.num_kb - 1 - kb : kb;
+            for (int kb = cur.kb0; kb < cur.kb1; ++kb) {
+                const int kc = reverse ? cur.kb0 + cur.kb1 - 1 - kb : kb;
                 if constexpr (T::kI4) {
                     // packed rows (64 bytes of K each) into the upper half of
                     // this CTA's ring stage once the MMAs have released it,
@@ -674,7 +770,9 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
             }
             if (aborted) break;
             if (leader) {  // the next work item
-                if (p.dynamic) {
+                if (p.sk) {
+                    if (!sk_item(p, unit, ++sk_i, cur)) cur.t = -1;
+                } else if (p.dynamic) {
                     int next = -1;
                     if (clc_pending) {
                         if (!wait_bounded(smem_u32(clcbar), clc_phase, abort_flag, p.timeout_ns,
@@ -690,9 +788,9 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
                         else
                             clc_live = false;  // nothing left to take over; never ask again
                     }
-                    t = next;
+                    cur = WorkItem{next, 0, p.num_kb, kItemFull, unit};
                 } else {
-                    t = t + units < num_work ? t + units : -1;
+                    cur = WorkItem{t + units < num_work ? t + units : -1, 0, p.num_kb, kItemFull, unit};
                 }
             }
         }
@@ -721,10 +819,12 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
                 aborted = true;
                 break;
             }
-            const int t = ring[q];
+            const WorkItem w = ring_get();
             ring_release();
             ring_next();
+            const int t = w.t;
             if (t < 0) break;
+            const int nkb = w.kb1 - w.kb0;            // k-blocks of this item
             const uint32_t idesc = t < p.split_from ? p.idesc : p.idesc_half;
             const int acc = local % T::kAccBufs;
             const uint32_t acc_phase = (local / T::kAccBufs) & 1;
@@ -774,7 +874,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
                 // half 0 first; the first ring-full of k-blocks goes into half
                 // 0 while half 1 is still being read, then the same k-blocks
                 // into half 1 (each half still accumulates in k order).
-                const int pre = p.num_kb < kStages ? p.num_kb : kStages;
+                const int pre = nkb < kStages ? nkb : kStages;
                 int st = stage;
                 uint32_t ph = phase;
                 for (int kb = 0; kb < pre; ++kb) {
@@ -803,7 +903,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
                 }
                 kb0 = pre;
             }
-            for (int kb = kb0; kb < p.num_kb; ++kb) {
+            for (int kb = kb0; kb < nkb; ++kb) {
                 if (!wait_bounded<kFullCluster>(smem_u32(&full[stage]), phase, abort_flag, p.timeout_ns,
                                                 (blockIdx.x << 8) | 0x30u | stage)) {
                     aborted = true;
@@ -855,22 +955,51 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
         const bool dequant = (kKind == kKindI8 || kKind == kKindI4) && p.scale_a != nullptr;
         const float combined = dequant ? __fmul_rn(*p.scale_a, *p.scale_b) : 0.f;
         uint32_t nstore = 0;  // TMA stores issued by this warp (selects the staging tile)
+        const int flag_idx = static_cast<int>(rank) * 4 + quarter;  // stream-K flag of this warp's rows
         int local = 0;
         for (;; ++local) {
             if (!wait_bounded_warp<kPair>(smem_u32(&qfull[q]), qph, abort_flag, p.timeout_ns,
                                           (blockIdx.x << 8) | 0x7Au | q))
                 break;
-            const int t = ring[q];
+            const WorkItem w = ring_get();
             __syncwarp();
             if (lane == 0) ring_release();
             ring_next();
+            const int t = w.t;
             if (t < 0) break;
+            // stream-K: a head's C values are a partial sum that the tail's
+            // epilogue adds to (TMA reduce-add) once the head has flagged them
+            const bool head = w.kind == kItemHead, tail = w.kind == kItemTail;
             const int acc = local % T::kAccBufs;
             const uint32_t acc_phase = (local / T::kAccBufs) & 1;
             if (!wait_bounded_warp(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.timeout_ns,
                                    (blockIdx.x << 8) | 0x40u | acc))
                 break;
             tc_fence_after();
+            if (tail) {
+                // the head's stores of these rows are complete once its flag
+                // carries this launch's tag (set long ago: heads run first)
+                unsigned int* flag = sk_flag(p, w.unit - 1, flag_idx);
+                uint64_t t0 = 0;
+                bool seen = false;
+                for (uint32_t i = 0;; ++i) {
+                    seen = ld_acquire_gpu(flag) == p.sk_epoch;
+                    if (__all_sync(0xffffffffu, seen)) break;
+                    if (i == 0) t0 = global_timer_ns();
+                    const bool stop = *abort_flag != 0u || global_timer_ns() - t0 > p.timeout_ns;
+                    if (__any_sync(0xffffffffu, stop)) {
+                        if (lane == 0 && *abort_flag == 0u)
+                            record_failure(abort_flag, (blockIdx.x << 8) | 0xD0u | flag_idx);
+                        break;
+                    }
+                }
+                if (!__all_sync(0xffffffffu, seen)) break;
+                if (lane == 0) {
+                    *flag = 0u;                   // consumed: ready for a later launch
+                    fence_proxy_async_global();   // the reduce-adds below come after the head's stores
+                }
+                __syncwarp();
+            }
             int b, tm, tn, half;
             work_coords(t, p.split_from, p.tiles_m, p.tiles_n, p.group_m, b, tm, tn, half);
             const int col0 = tn * kBN + (half < 0 ? 0 : half * (kBN / 2));
@@ -894,12 +1023,12 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
                     epi_convert<kAccF16, T::kI4>(va, dequant, combined);
                     epi_convert<kAccF16, T::kI4>(vb, dequant, combined);
                     epi_store_tma(&tmC, stile + (nstore & 1u) * 1024, stile_s + (nstore & 1u) * 4096, va, lane,
-                                  col, row0, b);
+                                  col, row0, b, tail);
                     if (p.n_extra > 0) epi_store_peers(p, stile + (nstore & 1u) * 1024, row0, col, cbase, lane);
                     ++nstore;
                     if (c + 32 < ncols && col + 32 < p.N) {
                         epi_store_tma(&tmC, stile + (nstore & 1u) * 1024, stile_s + (nstore & 1u) * 4096, vb,
-                                      lane, col + 32, row0, b);
+                                      lane, col + 32, row0, b, tail);
                         if (p.n_extra > 0)
                             epi_store_peers(p, stile + (nstore & 1u) * 1024, row0, col + 32, cbase, lane);
                         ++nstore;
@@ -958,6 +1087,17 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
                 }
             }
             }
+            if (head) {
+                // the partial is in C once this warp's stores have completed:
+                // flag it for the unit that finishes the tile
+                if (lane == 0) {
+                    bulk_wait_group_all();
+                    fence_proxy_async_global();
+                    __threadfence();
+                    st_release_gpu(sk_flag(p, w.unit, flag_idx), p.sk_epoch);
+                }
+                __syncwarp();
+            }
             if constexpr (!kWide) {
                 tc_fence_before();
                 __syncwarp();
@@ -997,16 +1137,16 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
             const bool got = wait_bounded_warp<kPair>(smem_u32(&qfull[q]), qph, abort_flag, p.timeout_ns,
                                                       (blockIdx.x << 8) | 0x7Bu);
             if (!named_barrier_and(1, kConv, got)) break;
-            const int t = ring[q];
+            const WorkItem w = ring_get();
             __syncwarp();
             if (lane == 0) ring_release();
             ring_next();
-            if (t < 0) break;
+            if (w.t < 0) break;
             int b, tm, tn, half;
-            work_coords(t, p.split_from, p.tiles_m, p.tiles_n, p.group_m, b, tm, tn, half);
+            work_coords(w.t, p.split_from, p.tiles_m, p.tiles_n, p.group_m, b, tm, tn, half);
             const int rows = T::kASub * kBM + (half < 0 ? T::kBRows : T::kBRows / 2);
             bool ok = true;
-            for (int kb = 0; kb < p.num_kb; ++kb) {
+            for (int kb = w.kb0; kb < w.kb1; ++kb) {
                 uint8_t* stage_ptr = smem + ss * T::kStageBytes;
                 const bool landed = wait_bounded_warp(smem_u32(&full_pk[ss]), sph, abort_flag, p.timeout_ns,
                                                       (blockIdx.x << 8) | 0xA0u | ss);

@@ -178,7 +178,8 @@ struct TileChoice {
 // (write C with plain stores instead of TMA stores), TCG_TAIL_SPLIT = 0 (no
 // half tiles in the last wave), TCG_STATIC_SCHEDULE = 1 (persistent units
 // with round-robin work items instead of cluster launch control), TCG_PDL = 0
-// (no programmatic dependent launch).
+// (no programmatic dependent launch), TCG_STREAM_K = 1 (stream-K split of
+// partial waves for integer kinds), TCG_S4_PREPASS = 1 (int4 in two passes).
 int env_int(const char* name, int dflt = 0)
 {
     const char* v = std::getenv(name);
@@ -427,12 +428,52 @@ tcg_status launch_gemm(DeviceState& dev, const void* A, const void* B, void* C, 
     static const int env_static = env_int("TCG_STATIC_SCHEDULE");
     p.dynamic = (!env_static && work > units && (kPair ? 2 : 1) * work <= 0x7fffffffLL) ? 1 : 0;
     p.wave_units = static_cast<int>(units);
-    const long long grid_units = p.dynamic ? work : (work < units ? work : units);
+    // Stream-K (integer kinds, two-CTA 512 x 256 tiles, one to four waves
+    // with a partial last one): every resident pair takes an equal share of
+    // the tiles' k-blocks laid end to end, so the last wave is not mostly
+    // idle.  A tile cut between two pairs: the pair with its first k-blocks
+    // (the head, its first item) stores its partial sums into C as usual and
+    // flags them; the pair with the rest (the tail, its last item) adds its
+    // sums onto them with TMA reduce-add stores.  Exact for integers; the
+    // floating-point kinds keep one k order per element and are not split.
+    // Static schedule (one persistent cluster per pair, all resident).
+    // Opt-in (TCG_STREAM_K=1): measured on B200 it loses to the data-parallel
+    // schedule at every shape tried -- the mainloop is bound by operand
+    // delivery (~0.8 us per k-block of a 512 x 256 tile with 74 pairs
+    // streaming), so giving the idle pairs of a partial wave work does not
+    // shorten the critical path, and the extra item boundary costs a drain.
+    p.sk = 0;
+    p.sk_units = 0;
+    p.sk_work = 0;
+    p.sk_epoch = 0;
+    p.sk_slot = 0;
+    static const int env_sk = env_int("TCG_STREAM_K", 0);
+    if constexpr (kShape == kShapePairWide) {
+        const double waves = static_cast<double>(tiles) / static_cast<double>(units);
+        const double rounds = static_cast<double>((tiles + units - 1) / units);
+        if ((kKind == kKindI8 || kKind == kKindI4) && epi.scale_a == nullptr && p.tma_store && env_sk &&
+            n_extra == 0 && tiles > units && tiles <= 4 * units && tiles % units != 0 &&
+            waves < 0.95 * rounds && p.num_kb >= 4 && units <= kSkMaxUnits) {
+            static std::atomic<unsigned int> epoch{0};
+            unsigned int e = ++epoch;
+            if (e == 0) e = ++epoch;  // 0 marks a consumed flag
+            p.sk = 1;
+            p.sk_units = static_cast<int>(units);
+            p.sk_work = tiles * p.num_kb;
+            p.sk_epoch = e;
+            p.sk_slot = static_cast<int>(e % kSkSlots);
+            p.split_from = static_cast<int>(tiles);
+            p.k_alternate = 0;
+            p.dynamic = 0;
+        }
+    }
+    const long long grid_units = p.sk ? units : p.dynamic ? work : (work < units ? work : units);
     static const int debug = env_int("TCG_DEBUG");
     if (debug)
         std::fprintf(stderr, "tcgemm: %s tile %dx%d stages %d units %lld grid %lld tiles %lld split_from %d group_m %d kalt %d %s\n",
                      kPair ? "pair" : (T::kWide ? "wide" : "single"), T::kTileM, kBN, kStages, units,
-                     grid_units, tiles, p.split_from, p.group_m, p.k_alternate, p.dynamic ? "dynamic" : "static");
+                     grid_units, tiles, p.split_from, p.group_m, p.k_alternate,
+                     p.sk ? "stream-k" : p.dynamic ? "dynamic" : "static");
     // Programmatic dependent launch: this grid may start while the previous
     // kernel on the stream finishes; it waits (griddepcontrol.wait) before
     // touching global memory.

@@ -3,7 +3,8 @@
 The environment switches are read once per process, so each configuration
 runs in a child process: static round-robin scheduling instead of cluster
 launch control (TCG_STATIC_SCHEDULE=1), plain stores instead of TMA stores
-for C (TCG_TMA_STORE=0), no column-half tail split (TCG_TAIL_SPLIT=0).  Each
+for C (TCG_TMA_STORE=0), no column-half tail split (TCG_TAIL_SPLIT=0), the
+stream-K split of partial waves (TCG_STREAM_K=1).  Each
 child multiplies multi-wave and single-wave int8 problems (bit-exact against
 the oracle) and an fp16 problem (bit-identical to the default
 configuration's result, which the parent computes), for every tile shape.
@@ -31,7 +32,7 @@ out_path = sys.argv[2]
 dev = "cuda:0"
 rng = np.random.default_rng(5)
 results = {}
-for (M, N, K) in ((3328, 3328, 256), (300, 520, 128)):
+for (M, N, K) in ((3328, 3328, 256), (300, 520, 128), (4096, 3072, 512)):
     A = rng.integers(-128, 128, (M, K), dtype=np.int8)
     B = rng.integers(-128, 128, (N, K), dtype=np.int8)
     ref = O.gemm_s8(A, B, threads=8)
@@ -50,6 +51,13 @@ for mode in (1, 2, 3, 4):
     T.set_cta_pair(mode)
     results[f"f16_{mode}"] = T.gemm_fp16(A16, B16).cpu().numpy()
 T.set_cta_pair(0)
+# 96 two-CTA 512 x 256 tiles on 74 pairs (fp16 keeps one k order per
+# element: never split, whatever the switch)
+Ah = rng.uniform(-1, 1, (4096, 512)).astype(np.float16)
+Bh = rng.uniform(-1, 1, (512, 3072)).astype(np.float16)
+A16, B16 = torch.from_numpy(Ah).to(dev), torch.from_numpy(Bh).to(dev)
+for acc in ("fp32", "fp16"):
+    results[f"f16_sk_{acc}"] = T.gemm_fp16(A16, B16, acc=acc).cpu().numpy()
 assert T.check_device_error() == 0
 np.savez(out_path, **results)
 print("child ok")
@@ -72,9 +80,9 @@ def default_result(tmp_path_factory):
 
 
 @pytest.mark.parametrize("env", [{"TCG_STATIC_SCHEDULE": "1"}, {"TCG_TMA_STORE": "0"},
-                                 {"TCG_TAIL_SPLIT": "0"},
+                                 {"TCG_TAIL_SPLIT": "0"}, {"TCG_STREAM_K": "1"},
                                  {"TCG_STATIC_SCHEDULE": "1", "TCG_TAIL_SPLIT": "0", "TCG_TMA_STORE": "0"}],
-                         ids=["static", "plain_stores", "no_tail_split", "all_off"])
+                         ids=["static", "plain_stores", "no_tail_split", "stream_k", "all_off"])
 def test_switch_keeps_results(env, default_result, tmp_path):
     res = _run(env, tmp_path, "switched")
     for key, ref in default_result.items():
