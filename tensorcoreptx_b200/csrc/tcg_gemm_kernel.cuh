@@ -871,37 +871,45 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
             int kb0 = 0;
             if constexpr (kWide) {
                 // Two-block shapes keep one tile in TMEM.  The epilogue frees
-                // half 0 first; the first ring-full of k-blocks goes into half
-                // 0 while half 1 is still being read, then the same k-blocks
-                // into half 1 (each half still accumulates in k order).
+                // half 0 first; while half 1 is still being read, k-blocks go
+                // into half 0 only (at most a ring-full: their stages stay
+                // held), and once half 1 is free the same k-blocks go into it
+                // (each half still accumulates in k order) and the tile
+                // continues with both halves per stage.  A half 1 that is
+                // already free (the first tile, or a drain that finished in
+                // time) skips the detour.
                 const int pre = nkb < kStages ? nkb : kStages;
                 int st = stage;
                 uint32_t ph = phase;
-                for (int kb = 0; kb < pre; ++kb) {
+                int held = 0;  // k-blocks issued into half 0 only
+                bool h1 = mbar_try_wait(smem_u32(&tempty[1]), acc_phase ^ 1u);
+                while (!h1 && held < pre) {
                     if (!wait_bounded<kFullCluster>(smem_u32(&full[st]), ph, abort_flag, p.timeout_ns,
                                                     (blockIdx.x << 8) | 0x30u | st)) {
                         aborted = true;
                         break;
                     }
                     tc_fence_after();
-                    issue(st, kb, 1);
+                    issue(st, held, 1);
+                    ++held;
                     if (++st == kStages) {
                         st = 0;
                         ph ^= 1u;
                     }
+                    h1 = mbar_try_wait(smem_u32(&tempty[1]), acc_phase ^ 1u);
                 }
                 if (aborted) break;
-                if (!wait_bounded(smem_u32(&tempty[1]), acc_phase ^ 1u, abort_flag, p.timeout_ns,
-                                  (blockIdx.x << 8) | 0x21u)) {
+                if (!h1 && !wait_bounded(smem_u32(&tempty[1]), acc_phase ^ 1u, abort_flag, p.timeout_ns,
+                                         (blockIdx.x << 8) | 0x21u)) {
                     aborted = true;
                     break;
                 }
                 tc_fence_after();
-                for (int kb = 0; kb < pre; ++kb) {
+                for (int kb = 0; kb < held; ++kb) {
                     issue(stage, kb, 2);
                     release_stage();
                 }
-                kb0 = pre;
+                kb0 = held;
             }
             for (int kb = kb0; kb < nkb; ++kb) {
                 if (!wait_bounded<kFullCluster>(smem_u32(&full[stage]), phase, abort_flag, p.timeout_ns,
