@@ -19,8 +19,10 @@ inputs resident in HBM (2 GiB of operands, larger than L2, so no flush is
 needed); ``e2e`` is the same metric through the public host-buffer API
 (``gemm_int8_host``): the step's A slice and B come from pinned host memory
 (with more than one GPU each rank copies 1/G of B and the ranks all-gather it
-over NVLink) and the C slice goes back, all inside the timed region.  Device
-time is measured with CUDA events on the launching stream, max over ranks.
+over NVLink) and the C slice goes back, all inside the timed region.  Its
+bound, ``e2e.copy_floor_ms``, is the same bytes copied with no GEMM (both
+directions at once, every rank at once).  Device time is measured with CUDA
+events on the launching stream, max over ranks.
 
 After the timed regions (never inside them) the run checks what it timed:
 every rank's whole C slice by Freivalds' check and four rows recomputed in
@@ -314,6 +316,48 @@ def timed(stream, fn, steps, warmup, barrier):
     return t0.elapsed_time(t1), [a.elapsed_time(b) for a, b in ev]
 
 
+def pcie_copy_floor(A_h, B_h, C_h, rank, world, dev, stream, barrier, max_over_ranks, reps=3):
+    """Milliseconds per step for the end-to-end step's host<->device bytes
+    alone: this rank's pinned A rows and its 1/world share of B copied in on
+    one stream while its pinned C rows are copied out on another, every rank
+    at once (they share the host's memory and PCIe).  Max over ranks; the
+    floor any host-buffer GEMM of this size reaches on this machine."""
+    import torch
+    rows, size = A_h.shape
+    share = size // world
+    B_mine = B_h[rank * share:(rank + 1) * share]
+    A_d = torch.empty_like(A_h, device=dev)
+    B_d = torch.empty_like(B_mine, device=dev)
+    C_d = torch.empty_like(C_h, device=dev)
+    s_in = torch.cuda.Stream(device=dev)
+
+    def step():
+        s_in.wait_stream(stream)
+        with torch.cuda.stream(s_in):
+            A_d.copy_(A_h, non_blocking=True)
+            B_d.copy_(B_mine, non_blocking=True)
+        with torch.cuda.stream(stream):
+            C_h.copy_(C_d, non_blocking=True)
+        stream.wait_stream(s_in)
+
+    step()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(reps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / reps
+    del A_d, B_d, C_d
+    torch.cuda.empty_cache()
+    return ms
+
+
 def gathered_legs(args, A, BT, r0, rows, size, world, dev, stream, barrier, max_over_ranks):
     """The optional all-gather of C (more than one GPU): the GEMM epilogue
     storing every tile into all ranks' C over NVLink (p2p), and block-cyclic
@@ -515,6 +559,8 @@ def run_ours(args):
     group = dist.group.WORLD if world > 1 else None
     del A, BT
     torch.cuda.empty_cache()
+    # before the end-to-end steps: it writes C_h, which they then overwrite
+    copy_floor_ms = pcie_copy_floor(A_h, B_h, C_h, rank, world, dev, stream, barrier, max_over_ranks)
 
     def e2e_step():
         # public host-buffer entry: pinned A slice and B in (1/G of B per rank
@@ -593,7 +639,13 @@ def run_ours(args):
                 "frac_of_sustained": achieved / (2.0 * float(peaks.get("bf16_tflops_sustained", 1400.0))),
             },
             "e2e": {"value": ops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms,
+                    "copy_floor_ms": copy_floor_ms,
+                    "frac_of_copy_floor": copy_floor_ms / e2e_ms,
+                    "copy_floor": "the same host<->device bytes per rank with no GEMM: pinned A slice and "
+                                  "this rank's share of B in, pinned C slice out, the two directions on "
+                                  "two streams at once (max over ranks)"},
             "gpu_launches": args.steps * (nccl_chunks if gather == "nccl" else 1),
             "clocks": ksum,
             "clock_norm": clock_norm,
