@@ -911,7 +911,11 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
                 }
                 kb0 = held;
             }
-            for (int kb = kb0; kb < nkb; ++kb) {
+            // two-block shapes: the last k-blocks (at most a ring-full) go
+            // into half 0 first, so half 0 is complete -- and the epilogue
+            // starts reading it -- while half 1 takes the same k-blocks
+            const int last = kWide ? (nkb - kb0 < kStages ? nkb - kb0 : kStages) : 0;
+            for (int kb = kb0; kb < nkb - last; ++kb) {
                 if (!wait_bounded<kFullCluster>(smem_u32(&full[stage]), phase, abort_flag, p.timeout_ns,
                                                 (blockIdx.x << 8) | 0x30u | stage)) {
                     aborted = true;
@@ -922,10 +926,41 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
                 release_stage();
             }
             if (aborted) break;
-            if constexpr (kPair)
-                umma_commit_pair(smem_u32(&tfull[acc]), 0x3);
-            else
-                umma_commit(smem_u32(&tfull[acc]));
+            if constexpr (kWide) {
+                int st = stage;
+                uint32_t ph = phase;
+                for (int i = 0; i < last; ++i) {
+                    if (!wait_bounded<kFullCluster>(smem_u32(&full[st]), ph, abort_flag, p.timeout_ns,
+                                                    (blockIdx.x << 8) | 0x30u | st)) {
+                        aborted = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue(st, nkb - last + i, 1);
+                    if (++st == kStages) {
+                        st = 0;
+                        ph ^= 1u;
+                    }
+                }
+                if (aborted) break;
+                if constexpr (kPair)
+                    umma_commit_pair(smem_u32(&tfull[0]), 0x3);
+                else
+                    umma_commit(smem_u32(&tfull[0]));
+                for (int i = 0; i < last; ++i) {
+                    issue(stage, nkb - last + i, 2);
+                    release_stage();
+                }
+                if constexpr (kPair)
+                    umma_commit_pair(smem_u32(&tfull[1]), 0x3);
+                else
+                    umma_commit(smem_u32(&tfull[1]));
+            } else {
+                if constexpr (kPair)
+                    umma_commit_pair(smem_u32(&tfull[acc]), 0x3);
+                else
+                    umma_commit(smem_u32(&tfull[acc]));
+            }
         }
         // Tail: wait until both accumulators' last use has been released by
         // the epilogue(s), so no release arrives on this CTA after it exits.
@@ -1013,8 +1048,18 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
             const int col0 = tn * kBN + (half < 0 ? 0 : half * (kBN / 2));
             const int ncols = half < 0 ? kBN : kBN / 2;
             const long long cbase = static_cast<long long>(b) * p.batch_stride_c;
+            bool lost = false;  // a bounded wait for half 1 gave up
 #pragma unroll 1
             for (int h = 0; h < T::kASub; ++h) {  // wide tiles: the two 128-row halves
+            if (kWide && h == 1) {
+                // half 1 completes after half 0 (its last k-blocks are issued second)
+                if (!wait_bounded_warp(smem_u32(&tfull[1]), acc_phase, abort_flag, p.timeout_ns,
+                                       (blockIdx.x << 8) | 0x42u)) {
+                    lost = true;
+                    break;
+                }
+                tc_fence_after();
+            }
             const int row0 =
                 tm * T::kTileM + static_cast<int>(rank) * (T::kASub * kBM) + h * kBM + quarter * 32;
             const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
@@ -1095,6 +1140,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, kAccF16, kBMn, kBN, kStages,
                 }
             }
             }
+            if (lost) break;
             if (head) {
                 // the partial is in C once this warp's stores have completed:
                 // flag it for the unit that finishes the tile
