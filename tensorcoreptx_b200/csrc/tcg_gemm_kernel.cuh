@@ -9,7 +9,8 @@
 //   * scheduling: one cluster per work item, running clusters taking over
 //     not-yet-started ones in launch order with cluster launch control (or,
 //     for a single wave, persistent units round-robin);
-//   * warp specialisation, 192 threads:
+//   * warp specialisation, 192 threads (int4: eight converter warps more,
+//     widening packed operands in the ring stages):
 //       warp 0 lane 0  -- TMA producer: 128-byte-swizzled A and B tiles into a
 //                         kStages-deep shared-memory ring (full/empty
 //                         mbarriers); in the leader CTA also the scheduler;
