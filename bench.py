@@ -17,16 +17,20 @@ every rank, and the reference arm, reproduce exactly the rows they need.
 A "step" is one GEMM of each rank's slice.  ``value`` is whole-job TOPS with
 inputs resident in HBM (2 GiB of operands, larger than L2, so no flush is
 needed); ``e2e`` is the same metric through the public host-buffer API
-(``gemm_int8_host``): the step's A slice and B come from pinned host memory
+(``gemm_int8_host``): the step's rows of A and B come from pinned host memory
 (with more than one GPU each rank copies 1/G of B and the ranks all-gather it
-over NVLink) and the C slice goes back, all inside the timed region.  Its
+over NVLink) and the rows of C go back, all inside the timed region.  With
+more than one GPU, A, B and C are one host matrix each, shared by the ranks,
+and the rows of the end-to-end step are split by each rank's measured host
+throughput (``e2e.rows_per_rank``).  Its
 bound, ``e2e.copy_floor_ms``, is the same bytes copied with no GEMM (both
 directions at once, every rank at once).  Device time is measured with CUDA
 events on the launching stream, max over ranks.
 
 After the timed regions (never inside them) the run checks what it timed:
 every rank's whole C slice by Freivalds' check and four rows recomputed in
-float64 on the GPU, the end-to-end C against the resident C, and, at one GPU,
+float64 on the GPU, the end-to-end C (against the resident C at one GPU,
+each rank's end-to-end rows by Freivalds' check with more), and, at one GPU,
 the rows of the CPU-baseline sample against the reference's own
 cpu_gemm_int8 -- the ``parity`` object of the line.  At one GPU the line also
 carries the reported baselines: the reference's cpu_gemm_int8 and a blocked
@@ -438,10 +442,33 @@ def run_ours(args):
         return _max_over_ranks(x, device=dev)
 
     # inputs: this rank's rows of A and all of BT (N x K), generated on the
-    # host, kept pinned for the end-to-end leg and copied to the device once
+    # host, kept pinned for the end-to-end leg and copied to the device once.
+    # With more than one GPU, A, B and C live in host memory shared by the
+    # ranks (each rank generates its equal share of A's and B's rows), so
+    # the end-to-end step can hand rows to whichever GPUs have the fastest
+    # path to host memory.
     threads = max(1, host_threads() // world)
-    A_h = gen_rows(SEED_A, r0, r1, size, threads).pin_memory()
-    B_h = gen_rows(SEED_B, 0, size, size, threads).pin_memory()
+    shared = None
+    if world > 1:
+        import shutil
+        need = 6 * size * size  # A and B int8, C int32
+        try:
+            room = shutil.disk_usage("/dev/shm").free >= 1.1 * need
+        except OSError:
+            room = False
+        if max_over_ranks(0.0 if room else 1.0) == 0.0:
+            from tensorcoreptx_b200.dist import SharedHostTensor
+            shared = {"A": SharedHostTensor((size, size), torch.int8, tag="A"),
+                      "B": SharedHostTensor((size, size), torch.int8, tag="B"),
+                      "C": SharedHostTensor((size, size), torch.int32, tag="C")}
+            gen_rows(SEED_A, r0, r1, size, threads, out=shared["A"].tensor[r0:r1])
+            gen_rows(SEED_B, r0, r1, size, threads, out=shared["B"].tensor[r0:r1])
+            barrier()
+            A_h = shared["A"].tensor[r0:r1]
+            B_h = shared["B"].tensor
+    if shared is None:
+        A_h = gen_rows(SEED_A, r0, r1, size, threads).pin_memory()
+        B_h = gen_rows(SEED_B, 0, size, size, threads).pin_memory()
     A = A_h.to(dev)
     BT = B_h.to(dev)
     C = torch.empty(rows, size, dtype=torch.int32, device=dev)
@@ -555,22 +582,57 @@ def run_ours(args):
         gathered = gathered_legs(args, A, BT, r0, rows, size, world, dev, stream, barrier, max_over_ranks)
 
     # ---- end-to-end through the public API: pinned host in, pinned host out
-    C_h = torch.empty(rows, size, dtype=torch.int32).pin_memory()
     group = dist.group.WORLD if world > 1 else None
     del A, BT
     torch.cuda.empty_cache()
-    # before the end-to-end steps: it writes C_h, which they then overwrite
-    copy_floor_ms = pcie_copy_floor(A_h, B_h, C_h, rank, world, dev, stream, barrier, max_over_ranks)
+    split = [shard_rows(size, world, k, align=256) for k in range(world)]
+    if shared is not None:
+        C_all = shared["C"].tensor
+    else:
+        C_h = torch.empty(rows, size, dtype=torch.int32).pin_memory()
 
-    def e2e_step():
-        # public host-buffer entry: pinned A slice and B in (1/G of B per rank
-        # plus an NVLink all-gather when G > 1), pinned C slice out, row x
-        # column blocks of C pipelined against the copies
-        T.gemm_int8_host(A_h, B_h, out=C_h, chunks=8, group=group)
+    def e2e_step(a0, a1):
+        # public host-buffer entry: pinned rows of A and B in (1/G of B per
+        # rank plus an NVLink all-gather when G > 1), pinned rows of C out,
+        # row x column blocks of C pipelined against the copies
+        if shared is not None:
+            T.gemm_int8_host(shared["A"].tensor[a0:a1], B_h, out=C_all[a0:a1], chunks=8, group=group)
+        else:
+            T.gemm_int8_host(A_h, B_h, out=C_h, chunks=8, group=group)
+
+    calib = []
+    if shared is not None:
+        # The ranks' paths to host memory differ (on some nodes half the GPUs
+        # reach it at a fraction of the others' rate), so the rows of the
+        # end-to-end step go to the ranks in proportion to the rate each
+        # reaches on the step itself: a few damped rounds from equal shares.
+        from tensorcoreptx_b200.dist import rebalance_rows
+        for _ in range(5):
+            a0, a1 = split[rank]
+            c0 = torch.cuda.Event(enable_timing=True)
+            c1 = torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                c0.record(stream)
+                e2e_step(a0, a1)
+                c1.record(stream)
+            torch.cuda.synchronize()
+            mine = torch.tensor([c0.elapsed_time(c1)], dtype=torch.float64, device=dev)
+            every = torch.empty(world, dtype=torch.float64, device=dev)
+            dist.all_gather_into_tensor(every, mine)
+            secs = every.tolist()
+            calib.append({"rows": [b1 - b0 for b0, b1 in split], "ms": [round(x, 2) for x in secs]})
+            split = rebalance_rows(size, split, secs)
+    a0, a1 = split[rank]
+    # before the end-to-end steps: it writes C rows, which they then overwrite
+    if shared is not None:
+        copy_floor_ms = pcie_copy_floor(shared["A"].tensor[a0:a1], B_h, C_all[a0:a1], rank, world, dev, stream,
+                                        barrier, max_over_ranks)
+    else:
+        copy_floor_ms = pcie_copy_floor(A_h, B_h, C_h, rank, world, dev, stream, barrier, max_over_ranks)
 
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):
-            e2e_step()
+            e2e_step(a0, a1)
     stream.synchronize()
     e2e_steps = max(3, min(args.steps, 10))
     barrier()
@@ -581,15 +643,28 @@ def run_ours(args):
     with torch.cuda.stream(stream):
         e0.record(stream)
         for _ in range(e2e_steps):
-            e2e_step()
+            e2e_step(a0, a1)
         e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     clocks.mark(None)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
-    h2d = rows * size + (size * size // world if world > 1 else size * size)
-    d2h = rows * size * 4
-    e2e_ok = bool(torch.equal(C_h.to(dev), C))
+    # bytes of the whole job per step: A and B once, C once
+    h2d = 2 * size * size
+    d2h = 4 * size * size
+    if shared is not None:
+        # this rank's end-to-end rows: Freivalds' check against its rows of A
+        # and B, plus its first and last row recomputed in float64
+        A_chk = shared["A"].tensor[a0:a1].to(dev)
+        B_chk = B_h.to(dev)
+        C_chk = C_all[a0:a1].to(dev)
+        e2e_ok = freivalds_int8(A_chk, B_chk, C_chk, trials=2, seed=100 + rank)
+        last = sorted({0, a1 - a0 - 1})
+        e2e_ok = e2e_ok and bool(torch.equal(rows_int8(A_chk, B_chk, last), C_chk[last]))
+        del A_chk, B_chk, C_chk
+        C_h = C_all[r0:r1]
+    else:
+        e2e_ok = bool(torch.equal(C_h.to(dev), C))
     del C
     torch.cuda.empty_cache()
 
@@ -597,11 +672,12 @@ def run_ours(args):
         clocks.stop()
     bad = max_over_ranks(0.0 if (fv_ok and rows_ok and e2e_ok) else 1.0)
     parity = {"freivalds_trials": 2, "freivalds_pass": fv_ok, "rows_fp64_device": len(chk_rows),
-              "rows_fp64_device_pass": rows_ok, "e2e_equals_resident": e2e_ok,
+              "rows_fp64_device_pass": rows_ok, "e2e_pass": e2e_ok,
               "all_ranks_pass": bad == 0.0,
               "what": "every rank: its whole C slice by Freivalds' check (C x == A (B^T x), exact in "
                       "float64), rows 0, 1, last-1, last recomputed in float64 on the GPU, and the "
-                      "end-to-end C equal to the resident C"}
+                      "end-to-end C: equal to the resident C at one GPU; with more GPUs each rank's "
+                      "end-to-end rows by Freivalds' check and their first and last row in float64"}
     parity["pass"] = parity["all_ranks_pass"]
 
     result = None
@@ -640,12 +716,16 @@ def run_ours(args):
             },
             "e2e": {"value": ops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "bytes": "whole job per step: A and B in once, C out once",
+                    "host_buffers": "private" if shared is None else "shared by the ranks (/dev/shm, pinned)",
+                    "rows_per_rank": [b1 - b0 for b0, b1 in split],
+                    "balance_rounds": calib,
                     "ms_per_step": e2e_ms,
                     "copy_floor_ms": copy_floor_ms,
                     "frac_of_copy_floor": copy_floor_ms / e2e_ms,
-                    "copy_floor": "the same host<->device bytes per rank with no GEMM: pinned A slice and "
-                                  "this rank's share of B in, pinned C slice out, the two directions on "
-                                  "two streams at once (max over ranks)"},
+                    "copy_floor": "the same host<->device bytes per rank with no GEMM: the rank's pinned "
+                                  "rows of A and its share of B in, its pinned rows of C out, the two "
+                                  "directions on two streams at once (max over ranks)"},
             "gpu_launches": args.steps * (nccl_chunks if gather == "nccl" else 1),
             "clocks": ksum,
             "clock_norm": clock_norm,
@@ -657,6 +737,9 @@ def run_ours(args):
 
     if world > 1:
         dist.barrier()
+        if shared is not None:
+            for sh in shared.values():
+                sh.close()
         dist.destroy_process_group()
     return result, (A_h, B_h, C_h)
 

@@ -173,6 +173,15 @@ tcg_status tcg_gemm_s4_static(const int8_t* A_packed, const int8_t* BT_packed, i
 tcg_status tcg_copy_2d_async(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width_bytes,
                              size_t height, void* stream);
 
+/* Page-lock a host range the caller has mapped (for example a POSIX shared
+ * memory segment every process of a job maps) so that copies between it and
+ * any GPU run as DMA, like pinned memory from cudaHostAlloc
+ * (cudaHostRegister, portable to every device).  Used by the multi-process
+ * host-buffer GEMM, whose ranks read A and B from, and write C to, one shared
+ * host matrix.  tcg_host_unregister undoes it before the range is unmapped. */
+tcg_status tcg_host_register(void* ptr, size_t bytes);
+tcg_status tcg_host_unregister(void* ptr);
+
 /* Device-side failure word.  Every wait inside the GEMM kernel is bounded
  * (default 2 s, tcg_set_wait_timeout_ns); on expiry the kernel records
  * (code << 32 | detail) here, drains its own copies in flight, frees its

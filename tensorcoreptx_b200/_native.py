@@ -41,6 +41,8 @@ SIGNATURES = {
     "tcg_quantize_absmax_s4": (C.c_int, [_p, _p, _i, _i, _p, _p]),
     "tcg_gemm_s4_static": (C.c_int, [_p, _p, _p, _i, _i, _i, _i, _p]),
     "tcg_copy_2d_async": (C.c_int, [_p, _sz, _p, _sz, _sz, _sz, _p]),
+    "tcg_host_register": (C.c_int, [_p, _sz]),
+    "tcg_host_unregister": (C.c_int, [_p]),
     "tcg_check_device_error": (C.c_int, [_p, C.POINTER(C.c_uint64)]),
     "tcg_set_wait_timeout_ns": (None, [C.c_uint64]),
     "tcg_selftest_wait_timeout": (C.c_int, [C.c_uint64, _p]),

@@ -999,6 +999,20 @@ tcg_status tcg_copy_2d_async(void* dst, size_t dpitch, const void* src, size_t s
     return e == cudaSuccess ? TCG_SUCCESS : cuda_fail(e);
 }
 
+tcg_status tcg_host_register(void* ptr, size_t bytes)
+{
+    if (!ptr || bytes == 0) return TCG_ERR_ARG;
+    cudaError_t e = cudaHostRegister(ptr, bytes, cudaHostRegisterPortable);
+    return e == cudaSuccess ? TCG_SUCCESS : cuda_fail(e);
+}
+
+tcg_status tcg_host_unregister(void* ptr)
+{
+    if (!ptr) return TCG_ERR_ARG;
+    cudaError_t e = cudaHostUnregister(ptr);
+    return e == cudaSuccess ? TCG_SUCCESS : cuda_fail(e);
+}
+
 tcg_status tcg_selftest_wait_timeout(uint64_t timeout_ns, void* stream)
 {
     DeviceState* dev;

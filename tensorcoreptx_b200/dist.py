@@ -32,6 +32,97 @@ def shard_rows(M: int, world: int, rank: int, align: int = 1) -> tuple[int, int]
     return min(M, u0 * align), min(M, u1 * align)
 
 
+def balanced_rows(M: int, rates, align: int = 256) -> list[tuple[int, int]]:
+    """Split M rows into len(rates) consecutive ranges, range i about
+    proportional to rates[i] (rows per second that rank i moves between host
+    and device), in whole blocks of `align` rows (the last range ends at M).
+    Every rank gets at least one block while M has one per rank, because the
+    host-buffer GEMM of a process group needs rows on every rank."""
+    n = len(rates)
+    if n < 1:
+        raise ValueError("no ranks")
+    w = [max(float(r), 0.0) for r in rates]
+    if sum(w) <= 0.0:
+        w = [1.0] * n
+    units = -(-M // align)
+    floor_units = 1 if units >= n else 0
+    free = units - floor_units * n
+    tot = sum(w)
+    share = [free * x / tot for x in w]
+    got = [int(x) for x in share]
+    # largest remainders take the blocks left over
+    for i in sorted(range(n), key=lambda i: share[i] - got[i], reverse=True)[:free - sum(got)]:
+        got[i] += 1
+    out, u = [], 0
+    for i in range(n):
+        u1 = u + floor_units + got[i]
+        out.append((min(M, u * align), min(M, u1 * align)))
+        u = u1
+    return out
+
+
+def rebalance_rows(M: int, split, seconds, align: int = 256, damping: float = 0.5) -> list[tuple[int, int]]:
+    """The next split after a step in which rank i took seconds[i] for the
+    rows split[i]: each rank's rate (rows per second) sets its share, and
+    the new shares are moved only `damping` of the way from the old ones, so
+    that ranks coupled by collectives settle instead of oscillating."""
+    rows = [r1 - r0 for r0, r1 in split]
+    rates = [r / max(t, 1e-9) for r, t in zip(rows, seconds)]
+    tot_r = sum(rates) or 1.0
+    target = [M * x / tot_r for x in rates]
+    mixed = [(1.0 - damping) * r + damping * t for r, t in zip(rows, target)]
+    return balanced_rows(M, mixed, align)
+
+
+class SharedHostTensor:
+    """One host tensor mapped by every rank of a process group (a POSIX
+    shared-memory segment), page-locked in each process for DMA.
+
+    Lets the ranks of one node exchange rows of A, B and C through host
+    memory: whichever GPU has the fastest path to host memory can read or
+    write any rows.  Rank 0 creates the segment under a name drawn for this
+    job and removes the name once every rank has mapped it, so nothing stays
+    behind in /dev/shm when the job ends.  `pin=False` maps it without
+    page-locking (CPU-only use).  Collective: every rank of `group` makes the
+    same call.  close() unpins it; the mapping goes with the last reference.
+    """
+
+    def __init__(self, shape, dtype: torch.dtype, group=None, tag: str = "buf", pin: bool = True,
+                 root: str = "/dev/shm"):
+        import os
+        import uuid
+
+        rank = dist.get_rank(group)
+        self.shape = tuple(int(d) for d in shape)
+        numel = 1
+        for d in self.shape:
+            numel *= d
+        self.nbytes = numel * torch.empty((), dtype=dtype).element_size()
+        names = [os.path.join(root, f"tcg_{tag}_{uuid.uuid4().hex}") if rank == 0 else None]
+        src = dist.get_global_rank(group, 0) if group is not None else 0
+        dist.broadcast_object_list(names, src=src, group=group)
+        path = names[0]
+        if rank == 0:
+            with open(path, "wb") as f:
+                f.truncate(self.nbytes)
+        dist.barrier(group)
+        self.tensor = torch.from_file(path, shared=True, size=numel, dtype=dtype).view(self.shape)
+        dist.barrier(group)
+        if rank == 0:
+            os.unlink(path)
+        self.pinned = False
+        if pin and self.nbytes > 0:
+            from . import _native as nat
+            nat.check("tcg_host_register", nat.lib().tcg_host_register(self.tensor.data_ptr(), self.nbytes))
+            self.pinned = True
+
+    def close(self):
+        if self.pinned:
+            from . import _native as nat
+            nat.check("tcg_host_unregister", nat.lib().tcg_host_unregister(self.tensor.data_ptr()))
+            self.pinned = False
+
+
 def max_over_ranks(x: float, device: Optional[torch.device] = None, group=None) -> float:
     """Maximum of a host scalar over all ranks (identity when not distributed)."""
     if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size(group) == 1:

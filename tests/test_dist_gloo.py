@@ -15,8 +15,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from tensorcoreptx_b200.dist import (cyclic_row_blocks, gathered_gemm_int8, max_over_ranks, shard_rows,
-                                     sharded_gemm_int8)
+from tensorcoreptx_b200.dist import (SharedHostTensor, balanced_rows, cyclic_row_blocks, gathered_gemm_int8,
+                                     max_over_ranks, rebalance_rows, shard_rows, sharded_gemm_int8)
 
 
 def _free_port():
@@ -171,3 +171,79 @@ def test_rank_leaving_becomes_an_error():
     what, dt = results[0]
     assert what != "no error", "collective with a departed rank returned normally"
     assert dt < 60, dt
+
+
+# ------------------------------------------ host-bandwidth-balanced rows --
+
+def _check_split(split, M, n, align):
+    assert len(split) == n
+    assert split[0][0] == 0 and split[-1][1] == M
+    for (a0, a1), (b0, b1) in zip(split, split[1:]):
+        assert a1 == b0
+    for r0, r1 in split:
+        assert r1 >= r0
+        assert r0 % align == 0 or r0 == M
+    if -(-M // align) >= n:
+        assert all(r1 > r0 for r0, r1 in split)
+
+
+def test_balanced_rows_partition_and_proportion():
+    for M in (0, 1, 300, 2048, 32768, 32768 + 100):
+        for rates in ([1.0], [1, 1], [1, 3], [5, 1, 1, 1], [0, 0, 1], [1] * 8, [18, 18, 18, 18, 44, 44, 44, 44]):
+            split = balanced_rows(M, rates, 256)
+            _check_split(split, M, len(rates), 256)
+    # proportional within one block
+    split = balanced_rows(32768, [18, 18, 18, 18, 44, 44, 44, 44], 256)
+    rows = [r1 - r0 for r0, r1 in split]
+    assert sum(rows) == 32768
+    for r, w in zip(rows, [18] * 4 + [44] * 4):
+        assert abs(r - 32768 * w / 248) <= 256 + 1e-9
+    # equal rates: equal rows
+    assert [r1 - r0 for r0, r1 in balanced_rows(32768, [2.0] * 8)] == [4096] * 8
+
+
+def test_rebalance_rows_settles_on_rate_shares():
+    """A model of ranks whose seconds per row differ 3:1: repeated
+    rebalancing converges to the split that equalises their times."""
+    M, n = 32768, 4
+    cost = [3.0, 3.0, 1.0, 1.0]  # seconds per row (arbitrary units)
+    split = balanced_rows(M, [1] * n)
+    for _ in range(12):
+        secs = [(r1 - r0) * c for (r0, r1), c in zip(split, cost)]
+        split = rebalance_rows(M, split, secs)
+        _check_split(split, M, n, 256)
+    secs = [(r1 - r0) * c for (r0, r1), c in zip(split, cost)]
+    assert max(secs) / min(secs) < 1.1
+
+
+def _worker_shared(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        sh = SharedHostTensor((world * 4, 8), torch.int32, tag="test", pin=False)
+        sh.tensor[rank * 4:(rank + 1) * 4] = rank + 1  # each rank writes its rows
+        dist.barrier()
+        want = torch.arange(1, world + 1, dtype=torch.int32).repeat_interleave(4)[:, None].expand(world * 4, 8)
+        ok = bool(torch.equal(sh.tensor, want))  # every rank sees every rank's rows
+        sh.close()
+        dist.destroy_process_group()
+        q.put((rank, ok, ""))
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, False, repr(e)))
+
+
+def test_shared_host_tensor_is_one_buffer_for_all_ranks():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    before = set(os.listdir("/dev/shm"))
+    procs = [ctx.Process(target=_worker_shared, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok, err in sorted(results):
+        assert ok, (rank, err)
+    # the segment's name was removed once every rank had mapped it
+    assert not [f for f in set(os.listdir("/dev/shm")) - before if f.startswith("tcg_test_")]

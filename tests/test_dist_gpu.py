@@ -2,7 +2,8 @@
 rank's gathered C -- one all-gather after the GEMM, block-cyclic blocks
 gathered while the next multiplies, and the GEMM epilogue's peer stores --
 equals the single-GPU product of the full matrices; so does the host-buffer
-GEMM of each rank's rows with B copied in halves and all-gathered."""
+GEMM of each rank's rows with B copied in halves and all-gathered, also with
+A, B and C in host memory shared by the ranks and unequal row shares."""
 import os
 import socket
 
@@ -65,6 +66,27 @@ def _worker(rank, world, port, q):
             C_h = T.gemm_int8_host(A_h, BT_h, chunks=chunks, group=dist.group.WORLD)
             torch.cuda.synchronize()
             ok = ok and bool(torch.equal(C_h, full[r0:r1].cpu()))
+        # the same with A, B and C in host memory shared by the ranks and
+        # unequal row shares (as the end-to-end step balances them): every
+        # rank's rows land in the one shared C, which then equals the product
+        from tensorcoreptx_b200.dist import SharedHostTensor, balanced_rows
+        sh = {k: SharedHostTensor(shape, dt, tag=k) for k, shape, dt in
+              (("A", (M, K), torch.int8), ("B", (N, K), torch.int8), ("C", (M, N), torch.int32))}
+        if rank == 0:
+            sh["A"].tensor.copy_(A.cpu())
+            sh["B"].tensor.copy_(BT.cpu())
+        dist.barrier()
+        for rates in ([1.0, 3.0], [2.0, 1.0]):
+            a0, a1 = balanced_rows(M, rates, 128)[rank]  # 384 / 640 rows: unequal, not 256-aligned
+            sh["C"].tensor[a0:a1].fill_(-1)
+            T.gemm_int8_host(sh["A"].tensor[a0:a1], sh["B"].tensor, out=sh["C"].tensor[a0:a1], chunks=2,
+                             group=dist.group.WORLD)
+            torch.cuda.synchronize()
+            dist.barrier()
+            ok = ok and bool(torch.equal(sh["C"].tensor, full.cpu()))
+            dist.barrier()
+        for v in sh.values():
+            v.close()
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, ok, ""))
