@@ -32,30 +32,35 @@ def shard_rows(M: int, world: int, rank: int, align: int = 1) -> tuple[int, int]
     return min(M, u0 * align), min(M, u1 * align)
 
 
-def balanced_rows(M: int, rates, align: int = 256) -> list[tuple[int, int]]:
+def balanced_rows(M: int, rates, align: int = 256, active=None) -> list[tuple[int, int]]:
     """Split M rows into len(rates) consecutive ranges, range i about
     proportional to rates[i] (rows per second that rank i moves between host
-    and device), in whole blocks of `align` rows (the last range ends at M).
-    Every rank gets at least one block while M has one per rank, because the
-    host-buffer GEMM of a process group needs rows on every rank."""
+    and device), in whole blocks of `align` rows (the last non-empty range
+    ends at M).  Ranks with active[i] False get an empty range; every active
+    rank gets at least one block while M has one per active rank."""
     n = len(rates)
     if n < 1:
         raise ValueError("no ranks")
-    w = [max(float(r), 0.0) for r in rates]
+    act = [True] * n if active is None else [bool(x) for x in active]
+    if not any(act):
+        raise ValueError("no active rank")
+    w = [max(float(r), 0.0) if a else 0.0 for r, a in zip(rates, act)]
     if sum(w) <= 0.0:
-        w = [1.0] * n
+        w = [1.0 if a else 0.0 for a in act]
+    n_act = sum(act)
     units = -(-M // align)
-    floor_units = 1 if units >= n else 0
-    free = units - floor_units * n
+    floor_units = 1 if units >= n_act else 0
+    free = units - floor_units * n_act
     tot = sum(w)
     share = [free * x / tot for x in w]
     got = [int(x) for x in share]
     # largest remainders take the blocks left over
-    for i in sorted(range(n), key=lambda i: share[i] - got[i], reverse=True)[:free - sum(got)]:
+    for i in sorted((i for i in range(n) if act[i]), key=lambda i: share[i] - got[i],
+                    reverse=True)[:free - sum(got)]:
         got[i] += 1
     out, u = [], 0
     for i in range(n):
-        u1 = u + floor_units + got[i]
+        u1 = u + (floor_units + got[i] if act[i] else 0)
         out.append((min(M, u * align), min(M, u1 * align)))
         u = u1
     return out
@@ -65,13 +70,15 @@ def rebalance_rows(M: int, split, seconds, align: int = 256, damping: float = 0.
     """The next split after a step in which rank i took seconds[i] for the
     rows split[i]: each rank's rate (rows per second) sets its share, and
     the new shares are moved only `damping` of the way from the old ones, so
-    that ranks coupled by collectives settle instead of oscillating."""
+    that ranks coupled by collectives settle instead of oscillating.  Ranks
+    without rows stay without rows."""
     rows = [r1 - r0 for r0, r1 in split]
+    act = [r > 0 for r in rows]
     rates = [r / max(t, 1e-9) for r, t in zip(rows, seconds)]
     tot_r = sum(rates) or 1.0
     target = [M * x / tot_r for x in rates]
     mixed = [(1.0 - damping) * r + damping * t for r, t in zip(rows, target)]
-    return balanced_rows(M, mixed, align)
+    return balanced_rows(M, mixed, align, active=act)
 
 
 class SharedHostTensor:

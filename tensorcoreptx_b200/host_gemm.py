@@ -132,7 +132,9 @@ def gemm_int8_host(A: torch.Tensor, BT: torch.Tensor, out: torch.Tensor | None =
     chunk of BT from host memory and the chunk is all-gathered over the group
     (NCCL; NVLink between the GPUs of one box), so each byte of B crosses PCIe
     once per step instead of once per rank.  Every rank of the group must make
-    the same call (same N, K and chunks) in the same order."""
+    the same call (same N, K and chunks) in the same order; a rank may have no
+    rows (M = 0: it only takes part in gathering B), which lets a job keep the
+    rows on the GPUs with the fastest path to host memory."""
     _check_host(A, "A", torch.int8)
     _check_host(BT, "BT", torch.int8)
     _check(A.size(1) == BT.size(1), "A cols must equal BT cols (both = K)")
@@ -142,9 +144,10 @@ def gemm_int8_host(A: torch.Tensor, BT: torch.Tensor, out: torch.Tensor | None =
     _check_host(C, "out", torch.int32)
     _check(tuple(C.shape) == (M, N), "out must be M x N")
     if group is not None:
-        # the collectives follow the column chunks: every rank must reach them
-        _check(M > 0 and N > 0, "row-sharded use needs rows and columns on every rank")
-    if M == 0 or N == 0:
+        # the collectives follow the column chunks: every rank must reach
+        # them, also a rank without rows (it still copies its share of B)
+        _check(N > 0, "row-sharded use needs columns on every rank")
+    if N == 0 or (M == 0 and group is None):
         return C
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     blocks = _blocks_for(M, N, chunks)

@@ -177,7 +177,7 @@ def test_rank_leaving_becomes_an_error():
 
 def _check_split(split, M, n, align):
     assert len(split) == n
-    assert split[0][0] == 0 and split[-1][1] == M
+    assert split[0][0] == 0 and max(r1 for _, r1 in split) == M
     for (a0, a1), (b0, b1) in zip(split, split[1:]):
         assert a1 == b0
     for r0, r1 in split:
@@ -200,6 +200,14 @@ def test_balanced_rows_partition_and_proportion():
         assert abs(r - 32768 * w / 248) <= 256 + 1e-9
     # equal rates: equal rows
     assert [r1 - r0 for r0, r1 in balanced_rows(32768, [2.0] * 8)] == [4096] * 8
+    # inactive ranks get empty ranges, the others share all rows
+    act = [False, True, False, True, True, False, False, True]
+    split = balanced_rows(32768, [1.0] * 8, 256, active=act)
+    assert [r1 - r0 for r0, r1 in split] == [0, 8192, 0, 8192, 8192, 0, 0, 8192]
+    assert split[0] == (0, 0) and split[1] == (0, 8192) and split[2] == (8192, 8192)
+    nxt = rebalance_rows(32768, split, [1.0, 2.0, 1.0, 1.0, 1.0, 1.0, 1.0, 1.0])
+    assert [r1 - r0 > 0 for r0, r1 in nxt] == act  # inactive stay inactive
+    assert nxt[1][1] - nxt[1][0] < 8192  # the slow active rank gives rows away
 
 
 def test_rebalance_rows_settles_on_rate_shares():

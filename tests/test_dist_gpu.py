@@ -3,7 +3,8 @@ rank's gathered C -- one all-gather after the GEMM, block-cyclic blocks
 gathered while the next multiplies, and the GEMM epilogue's peer stores --
 equals the single-GPU product of the full matrices; so does the host-buffer
 GEMM of each rank's rows with B copied in halves and all-gathered, also with
-A, B and C in host memory shared by the ranks and unequal row shares."""
+A, B and C in host memory shared by the ranks and unequal row shares (one
+of them with no rows on rank 0)."""
 import os
 import socket
 
@@ -76,8 +77,10 @@ def _worker(rank, world, port, q):
             sh["A"].tensor.copy_(A.cpu())
             sh["B"].tensor.copy_(BT.cpu())
         dist.barrier()
-        for rates in ([1.0, 3.0], [2.0, 1.0]):
-            a0, a1 = balanced_rows(M, rates, 128)[rank]  # 384 / 640 rows: unequal, not 256-aligned
+        # 384 / 640 rows (unequal, not 256-aligned), and all rows on rank 1
+        # (rank 0 only takes part in gathering B)
+        for rates, act in (([1.0, 3.0], None), ([2.0, 1.0], None), ([1.0, 1.0], [False, True])):
+            a0, a1 = balanced_rows(M, rates, 128, active=act)[rank]
             sh["C"].tensor[a0:a1].fill_(-1)
             T.gemm_int8_host(sh["A"].tensor[a0:a1], sh["B"].tensor, out=sh["C"].tensor[a0:a1], chunks=2,
                              group=dist.group.WORLD)
