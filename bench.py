@@ -21,8 +21,10 @@ needed); ``e2e`` is the same metric through the public host-buffer API
 (with more than one GPU each rank copies 1/G of B and the ranks all-gather it
 over NVLink) and the rows of C go back, all inside the timed region.  With
 more than one GPU, A, B and C are one host matrix each, shared by the ranks,
-and the rows of the end-to-end step are split by each rank's measured host
-throughput (``e2e.rows_per_rank``).  Its
+and the rows of the end-to-end step go to the set of ranks (all, or the
+fastest half or quarter) that moved them fastest in calibration steps, split
+by each rank's measured throughput (``e2e.rows_per_rank``,
+``e2e.balance_rounds``); ranks without rows only help gather B.  Its
 bound, ``e2e.copy_floor_ms``, is the same bytes copied with no GEMM (both
 directions at once, every rank at once).  Device time is measured with CUDA
 events on the launching stream, max over ranks.
