@@ -1005,6 +1005,33 @@ def blocked_cpu_leg():
     return out
 
 
+def naive_reference_cpu_leg():
+    """The reference's own CPU GEMMs (src/data.cu cpu_gemm_fp16,
+    src/data_int8.cu cpu_gemm_int8, src/data_int4.cu cpu_gemm_int4, compiled
+    unchanged into oracle/_ref/) at 512^3 on one host thread, on the
+    reference's own seeded inputs (its generate_* functions): the naive loop
+    the reference checks its kernels with, for context beside the blocked
+    GEMM.  Empty when the reference was not built here."""
+    import numpy as np
+    from oracle import oracle as O
+    n = 512
+    out = {"threads": 1, "what": "reference cpu_gemm_* (naive i-j-k), one call each"}
+    for which, abytes, key, unit in (("fp16", 2 * n, "fp16_512", "tflops"), ("int8", n, "int8_512", "tops"),
+                                      ("int4", n // 2, "int4_512", "tops")):
+        L = O.ref_data_lib(which)
+        if L is None:
+            return {}
+        A = np.zeros(n * abytes, np.uint8)
+        B = np.zeros(n * abytes, np.uint8)
+        Cm = np.zeros(n * n, np.float32 if which == "fp16" else np.int32)
+        L.gen(A.ctypes.data, B.ctypes.data, n, n, n, 1)
+        t0 = time.perf_counter()
+        L.gemm(A.ctypes.data, B.ctypes.data, Cm.ctypes.data, n, n, n)
+        t = time.perf_counter() - t0
+        out[key] = {unit: 2 * n ** 3 / t / 1e12, "ms": t * 1e3}
+    return out
+
+
 def reference_kernels_leg():
     """The reference's GPU kernels recompiled unchanged for sm_100a
     (oracle/_ref/libref_<kernel>.so), timed on this B200 like ours: int8 and
@@ -1062,6 +1089,7 @@ def main():
             ex["reference_kernels_b200"] = reference_kernels_leg()
             if not args.no_cpu_baseline:
                 ex["cpu_blocked"] = blocked_cpu_leg()
+                ex["cpu_reference_naive"] = naive_reference_cpu_leg()
             result["extras"] = ex
         sys.stdout.flush()
         os.write(json_fd, (json.dumps(result) + "\n").encode())
