@@ -612,10 +612,9 @@ def run_ours(args):
         # proportion to the rate each reaches on the step itself (a few damped
         # rounds per set), and the set whose step ended soonest is kept.
         # Ranks without rows still take part in gathering B.
-        from tensorcoreptx_b200.dist import balanced_rows, rebalance_rows
+        from tensorcoreptx_b200.dist import choose_host_rows
 
-        def timed_rows(sp):
-            b0, b1 = sp[rank]
+        def timed_rows(b0, b1):
             c0 = torch.cuda.Event(enable_timing=True)
             c1 = torch.cuda.Event(enable_timing=True)
             with torch.cuda.stream(stream):
@@ -623,34 +622,9 @@ def run_ours(args):
                 e2e_step(b0, b1)
                 c1.record(stream)
             torch.cuda.synchronize()
-            mine = torch.tensor([c0.elapsed_time(c1)], dtype=torch.float64, device=dev)
-            every = torch.empty(world, dtype=torch.float64, device=dev)
-            dist.all_gather_into_tensor(every, mine)
-            return every.tolist()
+            return c0.elapsed_time(c1)
 
-        sizes = [world] + [k for k in (world // 2, world // 4) if k >= 1 and k != world]
-        rates = None
-        best = None
-        for k in dict.fromkeys(sizes):
-            if rates is None:
-                act = [True] * world
-            else:
-                top = sorted(range(world), key=lambda i: (-rates[i], i))[:k]
-                act = [i in top for i in range(world)]
-            sp = balanced_rows(size, [1.0] * world, 256, active=act)
-            ends = []
-            for r in range(3):
-                secs = timed_rows(sp)
-                calib.append({"rows": [b1 - b0 for b0, b1 in sp], "ms": [round(x, 2) for x in secs]})
-                ends.append((max(secs), sp))
-                if rates is None and r == 2:
-                    rates = [(b1 - b0) / max(t, 1e-9) for (b0, b1), t in zip(sp, secs)]
-                sp = rebalance_rows(size, sp, secs)
-            # the set's score: the better of its last two rounds
-            cand = min(ends[1:], key=lambda e: e[0])
-            if best is None or cand[0] < best[0]:
-                best = cand
-        split = best[1]
+        split, calib = choose_host_rows(size, timed_rows, device=dev, align=256, rounds=3)
     a0, a1 = split[rank]
     # before the end-to-end steps: it writes C rows, which they then overwrite
     if shared is not None:

@@ -81,6 +81,57 @@ def rebalance_rows(M: int, split, seconds, align: int = 256, damping: float = 0.
     return balanced_rows(M, mixed, align, active=act)
 
 
+def choose_host_rows(M: int, run_step: Callable[[int, int], float], group=None,
+                     device: Optional[torch.device] = None, align: int = 256, rounds: int = 3):
+    """Pick which ranks of `group` take which rows of an M-row host-buffer
+    step, by timing the step itself.  `run_step(r0, r1)` runs one step with
+    this rank's rows [r0, r1) and returns its time (any unit); every rank
+    calls this function with the same M, align and rounds.
+
+    The ranks' paths to host memory differ and share the host's bandwidth,
+    so for each candidate set -- all ranks, then the fastest half and the
+    fastest quarter by the rate each reached with all of them -- `rounds`
+    damped rounds move rows in proportion to each rank's measured rows per
+    time unit (rebalance_rows), and the split whose step ended soonest (the
+    better of its last two rounds) is returned with the log of every round:
+    (split, [{"rows": [...], "ms": [...]}, ...]).  Ranks outside the chosen
+    set get no rows."""
+    world = dist.get_world_size(group) if (dist.is_available() and dist.is_initialized()) else 1
+    rank = dist.get_rank(group) if world > 1 else 0
+
+    def gathered(t: float) -> list[float]:
+        if world == 1:
+            return [float(t)]
+        mine = torch.tensor([float(t)], dtype=torch.float64, device=device)
+        every = torch.empty(world, dtype=torch.float64, device=device)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        return every.tolist()
+
+    sizes = [world] + [k for k in (world // 2, world // 4) if k >= 1 and k != world]
+    rates = None
+    best = None
+    log = []
+    for k in dict.fromkeys(sizes):
+        if rates is None:
+            act = [True] * world
+        else:
+            top = sorted(range(world), key=lambda i: (-rates[i], i))[:k]
+            act = [i in top for i in range(world)]
+        sp = balanced_rows(M, [1.0] * world, align, active=act)
+        ends = []
+        for r in range(rounds):
+            secs = gathered(run_step(*sp[rank]))
+            log.append({"rows": [b1 - b0 for b0, b1 in sp], "ms": [round(x, 2) for x in secs]})
+            ends.append((max(secs), sp))
+            if rates is None and r == rounds - 1:
+                rates = [(b1 - b0) / max(t, 1e-9) for (b0, b1), t in zip(sp, secs)]
+            sp = rebalance_rows(M, sp, secs, align)
+        cand = min(ends[-2:], key=lambda e: e[0])
+        if best is None or cand[0] < best[0]:
+            best = cand
+    return best[1], log
+
+
 class SharedHostTensor:
     """One host tensor mapped by every rank of a process group (a POSIX
     shared-memory segment), page-locked in each process for DMA.

@@ -15,8 +15,9 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from tensorcoreptx_b200.dist import (SharedHostTensor, balanced_rows, cyclic_row_blocks, gathered_gemm_int8,
-                                     max_over_ranks, rebalance_rows, shard_rows, sharded_gemm_int8)
+from tensorcoreptx_b200.dist import (SharedHostTensor, balanced_rows, choose_host_rows, cyclic_row_blocks,
+                                     gathered_gemm_int8, max_over_ranks, rebalance_rows, shard_rows,
+                                     sharded_gemm_int8)
 
 
 def _free_port():
@@ -255,3 +256,49 @@ def test_shared_host_tensor_is_one_buffer_for_all_ranks():
         assert ok, (rank, err)
     # the segment's name was removed once every rank had mapped it
     assert not [f for f in set(os.listdir("/dev/shm")) - before if f.startswith("tcg_test_")]
+
+
+def _worker_choose(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        base = [1.0, 1.0, 3.0, 3.0]  # rows per time unit alone: ranks 0, 1 slow
+
+        def fake_step(r0, r1):
+            # a host whose total rate is 5, or 3 while a slow rank copies too,
+            # shared in proportion to the active ranks' own rates
+            rows = torch.tensor([r1 - r0], dtype=torch.int64)
+            every = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
+            dist.all_gather(every, rows)
+            act = [int(t.item()) > 0 for t in every]
+            cap = 3.0 if (act[0] or act[1]) else 5.0
+            tot = sum(b for b, a in zip(base, act) if a)
+            rate = base[rank] * min(1.0, cap / tot)
+            return (r1 - r0) / rate if r1 > r0 else 0.1
+
+        split, log = choose_host_rows(32768, fake_step, align=256, rounds=3)
+        rows = [b - a for a, b in split]
+        dist.destroy_process_group()
+        q.put((rank, rows, len(log)))
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, repr(e), 0))
+
+
+def test_choose_host_rows_keeps_the_fastest_set():
+    """With all four ranks the host moves 3 row units per time unit; with only
+    the two fast ranks it moves 5: the search must hand every row to ranks 2
+    and 3, equally, and every rank must return the same split."""
+    world = 4
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_choose, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=180) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    splits = {tuple(rows) if isinstance(rows, list) else rows for _, rows, _ in results}
+    assert len(splits) == 1, results
+    rows = list(next(iter(splits)))
+    assert rows == [0, 0, 16384, 16384], rows
+    assert all(n == 9 for _, _, n in results)  # 3 sets x 3 rounds
