@@ -1,5 +1,5 @@
 /* cpu_blocked.c -- cache-blocked, multi-threaded CPU GEMMs: the host-core
- * baseline reported beside the B200 numbers (BASELINE / TEST INFRASTRUCTURE,
+ * baseline reported beside the B200 numbers (baseline and test infrastructure,
  * never on the product path).
  *
  * The reference's own CPU GEMMs are naive triple loops, one thread

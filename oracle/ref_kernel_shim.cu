@@ -1,5 +1,5 @@
 // ref_kernel_shim.cu -- C entry point around one reference kernel file
-// (TEST / BASELINE INFRASTRUCTURE, compiled into oracle/_ref/ only).
+// (test and baseline infrastructure, compiled into oracle/_ref/ only).
 //
 // Each reference kernel file defines the same C++ symbol `launch_kernel`
 // (fp16: kernels/fp16_wmma.cu:92-102; int8/int4: kernels/int8_wmma.cu:135-145,
